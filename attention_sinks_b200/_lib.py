@@ -1,0 +1,262 @@
+"""ctypes binding of the C ABI in include/sinkcache_b200.h, plus torch-tensor wrappers.
+
+Every GPU operation of this package goes through these wrappers into the sm_100a library
+`lib/libsinkcache_b200.so`.  There is no other implementation: if the library is missing,
+the first call raises, it never falls back to PyTorch or the CPU.
+"""
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libsinkcache_b200.so")
+
+DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
+OP_APPEND, OP_EVICT, OP_ATTEND, OP_FUSED_STEP = 0, 1, 2, 3
+STATUS_WAIT_TIMEOUT = 1
+
+_DTYPE_CODE = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}
+
+EXPORTED_SYMBOLS = (
+    "sink_abi_version", "sink_strerror", "sink_workspace_bytes", "sink_plan", "sink_append",
+    "sink_evict_rerotate", "sink_decode_attention", "sink_fused_decode_step", "sink_read_status",
+)
+
+
+class KVBuffers(ctypes.Structure):
+    """sink_kv_buffers_t"""
+    _fields_ = [
+        ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("k_dtype", ctypes.c_int32), ("v_dtype", ctypes.c_int32),
+        ("batch", ctypes.c_int32), ("heads_kv", ctypes.c_int32),
+        ("slots", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+        ("k_stride_b", ctypes.c_int64), ("k_stride_h", ctypes.c_int64),
+        ("v_stride_b", ctypes.c_int64), ("v_stride_h", ctypes.c_int64),
+    ]
+
+
+class Rows(ctypes.Structure):
+    """sink_rows_t"""
+    _fields_ = [
+        ("data", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("heads", ctypes.c_int32),
+        ("n", ctypes.c_int32), ("pad_", ctypes.c_int32),
+        ("stride_b", ctypes.c_int64), ("stride_h", ctypes.c_int64), ("stride_t", ctypes.c_int64),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def _declare(lib):
+    i32, i64, sz, vp, fp = ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p
+    pkv, prows = ctypes.POINTER(KVBuffers), ctypes.POINTER(Rows)
+    pi32 = ctypes.POINTER(ctypes.c_int32)
+    sig = {
+        "sink_abi_version": (i32, []),
+        "sink_strerror": (ctypes.c_char_p, [i32]),
+        "sink_workspace_bytes": (sz, [i32] * 12),
+        "sink_plan": (i32, [i32] * 12 + [pi32] * 5),
+        "sink_append": (i32, [pkv, prows, prows, i32, vp]),
+        "sink_evict_rerotate": (i32, [pkv, i32, i32, i32, fp, fp, i32, vp, sz, vp]),
+        "sink_decode_attention": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, i64, vp, sz, vp]),
+        "sink_fused_decode_step": (i32, [pkv, prows, prows, prows, i32, i32, i32, i32, fp, fp, i32,
+                                         ctypes.c_float, vp, i64, i64, vp, sz, vp]),
+        "sink_read_status": (i32, [vp, vp, pi32]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype, fn.argtypes = res, args
+
+
+def lib():
+    """The loaded library.  Raises if it has not been built (there is no fallback)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"sinkcache_b200 CUDA library not found at {LIB_PATH}; build it with "
+                        "`python -m attention_sinks_b200.build`")
+                handle = ctypes.CDLL(LIB_PATH)
+                _declare(handle)
+                _lib = handle
+    return _lib
+
+
+def strerror(code: int) -> str:
+    return lib().sink_strerror(int(code)).decode()
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed ({rc}): {strerror(rc)}")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dtype]
+    except KeyError:
+        raise TypeError(f"sinkcache_b200 supports float32 / bfloat16 / float16, got {dtype}") from None
+
+
+def check_device(device: torch.device) -> None:
+    """The kernels run on CUDA devices only; there is no CPU implementation."""
+    if device.type != "cuda":
+        raise RuntimeError(f"sinkcache_b200 runs on CUDA devices only (got {device})")
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        check_device(t.device)
+
+
+def kv_desc(kbuf: torch.Tensor, vbuf: torch.Tensor) -> KVBuffers:
+    """Descriptor of [B, Hkv, slots, D] cache buffers (rows must be contiguous)."""
+    _require_cuda(kbuf, vbuf)
+    if kbuf.shape != vbuf.shape or kbuf.dim() != 4:
+        raise ValueError(f"K/V buffers must be [B, H, slots, D] of one shape, got {tuple(kbuf.shape)}, "
+                         f"{tuple(vbuf.shape)}")
+    d = kbuf.shape[-1]
+    for t in (kbuf, vbuf):
+        if t.stride(-1) != 1 or t.stride(-2) != d:
+            raise ValueError("cache buffers need contiguous rows (stride[-2] == head_dim, stride[-1] == 1)")
+    b, h, s, _ = kbuf.shape
+    return KVBuffers(kbuf.data_ptr(), vbuf.data_ptr(), dtype_code(kbuf.dtype), dtype_code(vbuf.dtype),
+                     b, h, s, d, kbuf.stride(0), kbuf.stride(1), vbuf.stride(0), vbuf.stride(1))
+
+
+def rows_desc(t: torch.Tensor) -> Rows:
+    """Descriptor of a [B, H, n, D] tensor with a unit last stride."""
+    _require_cuda(t)
+    if t.dim() != 4 or t.stride(-1) != 1:
+        raise ValueError(f"expected a [B, H, n, D] tensor with unit last stride, got {tuple(t.shape)} "
+                         f"strides {t.stride()}")
+    return Rows(t.data_ptr(), dtype_code(t.dtype), t.shape[1], t.shape[2], 0,
+                t.stride(0), t.stride(1), t.stride(2))
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+_sm_count = {}
+
+
+def sm_count(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _sm_count:
+        _sm_count[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _sm_count[idx]
+
+
+def workspace_bytes(op: int, batch: int, heads_kv: int, heads_q: int, head_dim: int,
+                    k_dtype: torch.dtype, v_dtype: torch.dtype, rows: int, n_sink: int,
+                    window: int, drop: int, num_sms: int) -> int:
+    n = lib().sink_workspace_bytes(op, batch, heads_kv, heads_q, head_dim, dtype_code(k_dtype),
+                                   dtype_code(v_dtype), rows, n_sink, window, drop, num_sms)
+    if n == 0:
+        raise ValueError("sinkcache_b200: unsupported shapes for the workspace query "
+                         f"(op={op}, B={batch}, Hkv={heads_kv}, Hq={heads_q}, D={head_dim}, "
+                         f"K={k_dtype}, V={v_dtype}, rows={rows})")
+    return int(n)
+
+
+def plan(op: int, batch: int, heads_kv: int, heads_q: int, head_dim: int, k_dtype: torch.dtype,
+         v_dtype: torch.dtype, rows: int, n_sink: int, window: int, drop: int, num_sms: int) -> dict:
+    out = [ctypes.c_int32() for _ in range(5)]
+    rc = lib().sink_plan(op, batch, heads_kv, heads_q, head_dim, dtype_code(k_dtype), dtype_code(v_dtype),
+                         rows, n_sink, window, drop, num_sms, *[ctypes.byref(o) for o in out])
+    _check(rc, "sink_plan")
+    keys = ("splits", "rows_per_split", "chunk_rows", "stages", "smem_bytes")
+    return {k: o.value for k, o in zip(keys, out)}
+
+
+class Workspace:
+    """Device scratch for the kernels (split partials, halo rows, status word), grown on
+    demand and reused.  A step captured in a CUDA graph keeps the pointer it saw, so
+    size it before capture (SinkLayer does, at lazy initialisation)."""
+
+    def __init__(self):
+        self.buf = None
+
+    def get(self, nbytes: int, device: torch.device) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
+            self.buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        return self.buf
+
+    def read_status(self) -> int:
+        """Status bits set by kernels since the last read (synchronises the stream)."""
+        if self.buf is None:
+            return 0
+        st = ctypes.c_int32(0)
+        _check(lib().sink_read_status(self.buf.data_ptr(), stream_handle(self.buf.device),
+                                      ctypes.byref(st)), "sink_read_status")
+        return st.value
+
+
+# ---------------------------------------------------------------------------- operations
+
+
+def append(kbuf: torch.Tensor, vbuf: torch.Tensor, k: torch.Tensor, v: torch.Tensor, row: int) -> None:
+    """kbuf[:, :, row:row+n] = k; vbuf[:, :, row:row+n] = v (cache.py:159-160)."""
+    kv = kv_desc(kbuf, vbuf)
+    rc = lib().sink_append(ctypes.byref(kv), ctypes.byref(rows_desc(k)), ctypes.byref(rows_desc(v)),
+                           int(row), stream_handle(kbuf.device))
+    _check(rc, "sink_append")
+
+
+def evict_rerotate(kbuf: torch.Tensor, vbuf: torch.Tensor, n_sink: int, window: int, drop: int,
+                   cos: torch.Tensor | None, sin: torch.Tensor | None, ws: Workspace) -> None:
+    """In-place shift of the window by `drop` rows, keys rotated by -drop (kernels.py:59-73)."""
+    kv = kv_desc(kbuf, vbuf)
+    b, h, _, d = kbuf.shape
+    need = workspace_bytes(OP_EVICT, b, h, h, d, kbuf.dtype, vbuf.dtype, 0, n_sink, window, drop,
+                           sm_count(kbuf.device))
+    buf = ws.get(need, kbuf.device)
+    rotate = cos is not None
+    rc = lib().sink_evict_rerotate(ctypes.byref(kv), n_sink, window, drop,
+                                   cos.data_ptr() if rotate else None, sin.data_ptr() if rotate else None,
+                                   1 if rotate else 0, buf.data_ptr(), buf.numel(),
+                                   stream_handle(kbuf.device))
+    _check(rc, "sink_evict_rerotate")
+
+
+def decode_attention(q: torch.Tensor, kbuf: torch.Tensor, vbuf: torch.Tensor, rows: int, scale: float,
+                     out: torch.Tensor, ws: Workspace) -> torch.Tensor:
+    """out[B, 1, Hq, D] = attention of q[B, Hq, 1, D] over kbuf/vbuf rows [0, rows)."""
+    kv = kv_desc(kbuf, vbuf)
+    b, h, _, d = kbuf.shape
+    need = workspace_bytes(OP_ATTEND, b, h, q.shape[1], d, kbuf.dtype, vbuf.dtype, rows, 0, 1, 0,
+                           sm_count(kbuf.device))
+    buf = ws.get(need, kbuf.device)
+    rc = lib().sink_decode_attention(ctypes.byref(rows_desc(q)), ctypes.byref(kv), int(rows), float(scale),
+                                     out.data_ptr(), out.stride(0), out.stride(2), buf.data_ptr(), buf.numel(),
+                                     stream_handle(kbuf.device))
+    _check(rc, "sink_decode_attention")
+    return out
+
+
+def fused_decode_step(kbuf: torch.Tensor, vbuf: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      q: torch.Tensor, n_sink: int, window: int, drop: int, append_row: int,
+                      cos: torch.Tensor | None, sin: torch.Tensor | None, scale: float,
+                      out: torch.Tensor, ws: Workspace) -> torch.Tensor:
+    """Evict `drop` rows (re-rotating keys), append (k, v) at `append_row`, attend q over rows
+    [0, append_row] -- one pass over the cache."""
+    kv = kv_desc(kbuf, vbuf)
+    b, h, _, d = kbuf.shape
+    need = workspace_bytes(OP_FUSED_STEP, b, h, q.shape[1], d, kbuf.dtype, vbuf.dtype, append_row + 1,
+                           n_sink, window, drop, sm_count(kbuf.device))
+    buf = ws.get(need, kbuf.device)
+    rotate = cos is not None
+    rc = lib().sink_fused_decode_step(
+        ctypes.byref(kv), ctypes.byref(rows_desc(k)), ctypes.byref(rows_desc(v)), ctypes.byref(rows_desc(q)),
+        n_sink, window, drop, append_row, cos.data_ptr() if rotate else None,
+        sin.data_ptr() if rotate else None, 1 if rotate else 0, float(scale), out.data_ptr(),
+        out.stride(0), out.stride(2), buf.data_ptr(), buf.numel(), stream_handle(kbuf.device))
+    _check(rc, "sink_fused_decode_step")
+    return out

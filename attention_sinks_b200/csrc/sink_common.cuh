@@ -1,0 +1,289 @@
+// Shared definitions of the sink-cache kernels: launch arguments, the split plan that host
+// and device both evaluate, PTX wrappers for mbarriers and bulk (TMA) copies, element
+// conversions.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sinkb200 {
+
+constexpr int kThreads = 128;                 // 4 warps per CTA
+constexpr int kWarps = kThreads / 32;
+constexpr int kPipeBytes = 98304;             // pipeline smem budget per CTA: 2 CTAs per SM
+constexpr int kBarrierBytes = 128;            // mbarriers in front of the stages
+constexpr int kSmemPerSM = 233472;            // B200: 228 KB shared memory per SM
+constexpr int kSmemReservedPerCTA = 1024;
+constexpr int kMaxSplits = 256;               // combine kernel keeps ns * G weights in smem
+constexpr int kMaxGroup = 8;
+
+__host__ __device__ inline int imin(int a, int b) { return a < b ? a : b; }
+__host__ __device__ inline int imax(int a, int b) { return a > b ? a : b; }
+
+// Arguments of one stream-kernel launch.  Output rows [row_begin, row_end) of every
+// (batch, kv-head) pair are split into `ns` contiguous splits of `rows_per_split` rows.
+// Output row r reads:
+//   - buffer row r + drop (or the halo copy of it)  if drop > 0 and n_sink <= r < n_sink+window
+//   - the new token (knew / vnew)                    if r == append_row
+//   - buffer row r                                   otherwise (sinks, or drop == 0)
+// and writes back (window rows when drop > 0, and the append row).
+struct StreamArgs {
+  char* kbuf;
+  char* vbuf;
+  int64_t k_sb, k_sh, v_sb, v_sh;  // element strides of batch / head; rows are contiguous
+  const char* knew;
+  const char* vnew;
+  int64_t kn_sb, kn_sh, vn_sb, vn_sh;
+  const char* q;
+  int64_t q_sb, q_sh;
+  char* out;
+  int64_t o_sb, o_sh;
+  const float* cos_tab;
+  const float* sin_tab;
+  int heads_kv, group;
+  int n_sink, window, drop, rotate;
+  int row_begin, row_end, append_row, written_end;
+  int ns, rows_per_split, halo_rows;
+  float scale_log2;
+  float* o_part;
+  float* m_part;
+  float* l_part;
+  char* halo_k;
+  char* halo_v;
+  int* status;
+};
+
+// Rows [a, e) of split j.
+__host__ __device__ inline void split_rows(int row_begin, int row_end, int rows_per_split, int j,
+                                           int& a, int& e) {
+  a = row_begin + j * rows_per_split;
+  e = imin(a + rows_per_split, row_end);
+}
+
+// Source rows of split j that another split of the same launch may overwrite before split j
+// reads them: they are copied to the halo workspace by a pre-pass.  [hlo, hhi) in buffer-row
+// space; empty when hlo >= hhi.  Split j's window sources are [max(a, s) + drop,
+// min(e, s + W) + drop); rows below e belong to split j itself (read before written, in
+// order); rows from e up to `written_end` (exclusive) are destinations of later splits.
+__host__ __device__ inline void halo_range(int n_sink, int window, int drop, int written_end,
+                                           int ns, int j, int a, int e, int& hlo, int& hhi) {
+  hlo = hhi = 0;
+  if (drop <= 0 || j >= ns - 1) return;
+  const int w0 = imax(a, n_sink), w1 = imin(e, n_sink + window);
+  if (w0 >= w1) return;
+  const int s0 = w0 + drop, s1 = w1 + drop;
+  const int lo = imax(s0, e), hi = imin(s1, written_end);
+  if (lo < hi) {
+    hlo = lo;
+    hhi = hi;
+  }
+}
+
+// ------------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for a phase of an mbarrier: false if the copies never landed (then the
+// caller records SINK_STATUS_WAIT_TIMEOUT and abandons its work instead of hanging).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+#pragma unroll 1
+  for (int i = 0; i < (1 << 20); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i >= 64) __nanosleep(256);
+  }
+  return false;
+}
+
+// global -> shared bulk copy, completion counted on `bar` in bytes.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// shared -> global bulk copy, tracked by bulk groups.
+__device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ------------------------------------------------------------------ element conversions
+
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float x) { return x; }
+  static __device__ __forceinline__ float from_f(float x) { return x; }
+  static __device__ __forceinline__ void load4(const float* p, float (&o)[4]) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    o[0] = v.x;
+    o[1] = v.y;
+    o[2] = v.z;
+    o[3] = v.w;
+  }
+  static __device__ __forceinline__ void store4(float* p, const float (&o)[4]) {
+    *reinterpret_cast<float4*>(p) = make_float4(o[0], o[1], o[2], o[3]);
+  }
+  static __device__ __forceinline__ void load8(const float* p, float (&o)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    o[0] = a.x;
+    o[1] = a.y;
+    o[2] = a.z;
+    o[3] = a.w;
+    o[4] = b.x;
+    o[5] = b.y;
+    o[6] = b.z;
+    o[7] = b.w;
+  }
+  // round-trip through the storage type (identity for float)
+  static __device__ __forceinline__ float round(float x) { return x; }
+};
+
+template <>
+struct Elem<__nv_bfloat16> {
+  using T = __nv_bfloat16;
+  static __device__ __forceinline__ float to_f(T x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ T from_f(float x) { return __float2bfloat16_rn(x); }
+  static __device__ __forceinline__ void load4(const T* p, float (&o)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    o[0] = a.x;
+    o[1] = a.y;
+    o[2] = b.x;
+    o[3] = b.y;
+  }
+  static __device__ __forceinline__ void store4(T* p, const float (&o)[4]) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(o[0], o[1]);
+    __nv_bfloat162 b = __floats2bfloat162_rn(o[2], o[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&a);
+    u.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = u;
+  }
+  static __device__ __forceinline__ void load8(const T* p, float (&o)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ float round(float x) {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  }
+};
+
+template <>
+struct Elem<__half> {
+  using T = __half;
+  static __device__ __forceinline__ float to_f(T x) { return __half2float(x); }
+  static __device__ __forceinline__ T from_f(float x) { return __float2half_rn(x); }
+  static __device__ __forceinline__ void load4(const T* p, float (&o)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    o[0] = a.x;
+    o[1] = a.y;
+    o[2] = b.x;
+    o[3] = b.y;
+  }
+  static __device__ __forceinline__ void store4(T* p, const float (&o)[4]) {
+    __half2 a = __floats2half2_rn(o[0], o[1]);
+    __half2 b = __floats2half2_rn(o[2], o[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&a);
+    u.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = u;
+  }
+  static __device__ __forceinline__ void load8(const T* p, float (&o)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
+};
+
+// Compile-time geometry of the stream kernel for one (K type, V type, head_dim).
+//   LPR lanes share one cache row: lane i of a row owns K dims [4i, 4i+4) and
+//   [D/2 + 4i, D/2 + 4i + 4) (the RoPE half-split partners) and V dims [8i, 8i + 8).
+//   A warp covers RPW rows per step; a chunk of T rows is 4 steps of all 4 warps.
+template <typename KT, typename VT, int D>
+struct StreamGeom {
+  static_assert(D == 64 || D == 128 || D == 256, "head_dim");
+  static constexpr int LPR = D / 8;
+  static constexpr int RPW = 32 / LPR;
+  static constexpr int STEPS = 4;
+  static constexpr int T = STEPS * kWarps * RPW;
+  static constexpr int KROW = D * (int)sizeof(KT);
+  static constexpr int VROW = D * (int)sizeof(VT);
+  static constexpr int STAGE = T * (KROW + VROW);
+  static constexpr int S0 = kPipeBytes / STAGE;
+  static constexpr int S = S0 < 2 ? 2 : (S0 > 4 ? 4 : S0);
+  static constexpr int SMEM = kBarrierBytes + S * STAGE;
+  // the end-of-split merge reuses the stage memory
+  static_assert(kWarps * kMaxGroup * (D + 2) * 4 <= S * STAGE, "merge scratch");
+};
+
+}  // namespace sinkb200

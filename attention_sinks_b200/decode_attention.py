@@ -1,0 +1,68 @@
+"""Split-K GQA decode attention for one query token, and the Transformers attention backend
+that drives the fused sink-cache decode step.
+
+`flash_decode` (src/sinkcache/decode_attention.py:102-130) runs the sm_100a kernels: each
+CTA streams one split of one (batch, kv-head) pair's rows through a bulk-copy (TMA)
+shared-memory pipeline, keeps an fp32 online softmax for the whole GQA group, and a second
+kernel merges the splits.  Keys may be float32 (the sink cache's storage, read directly:
+no bf16 copy of the cache per step) or the model dtype.
+
+`register(name)` (decode_attention.py:149-156) installs `decode_attention_forward` as a
+Transformers attention backend: one-token steps without a mask run on the kernels --
+fused with the cache update when the key view comes from a deferred SinkLayer step --
+and anything else (prefill chunks, masks) falls back to SDPA, as the reference does.
+"""
+
+import torch
+
+from . import _lib
+from .cache import pending_layer
+
+REGISTERED: set[str] = set()
+calls = {"decode_kernel": 0, "fused_step": 0, "sdpa_fallback": 0}
+
+
+def flash_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
+    """q [B, Hq, 1, D]; k, v [B, Hkv, L, D] with contiguous rows (views of a larger cache
+    buffer are fine).  Returns the attention output as [B, 1, Hq, D] in q's dtype."""
+    bsz, hq, q_len, dim = q.shape
+    if q_len != 1 or hq % k.shape[1]:
+        raise ValueError(f"flash_decode needs one query token and Hq % Hkv == 0, got q {tuple(q.shape)}, "
+                         f"k {tuple(k.shape)}")
+    out = torch.empty(bsz, 1, hq, dim, device=q.device, dtype=q.dtype)
+    ws = _lib.Workspace()  # per call, like the reference's partials: safe under graph capture
+    return _lib.decode_attention(q, k, v, k.shape[2], scale, out, ws)
+
+
+def decode_attention_forward(module, query, key, value, attention_mask, dropout=0.0, scaling=None, **kwargs):
+    """Transformers attention function (decode_attention.py:136-146): the sm_100a kernels
+    for one query token, SDPA otherwise."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    layer = pending_layer(key)
+    if query.shape[2] == 1 and attention_mask is None and query.is_cuda and not module.training:
+        scale = scaling if scaling is not None else query.shape[-1] ** -0.5
+        if layer is not None:
+            calls["fused_step"] += 1
+            return layer.run_pending(query, scale), None
+        calls["decode_kernel"] += 1
+        return flash_decode(query, key, value, scale), None
+    if layer is not None:
+        layer.materialize()
+    calls["sdpa_fallback"] += 1
+    if key.dtype != query.dtype:  # float32 key storage
+        key = key.to(query.dtype)
+    return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,
+                                  scaling=scaling, **kwargs)
+
+
+def register(name: str = "sdpa_decode") -> str:
+    """Register the backend; then load the model with attn_implementation=name
+    (decode_attention.py:149-156)."""
+    from transformers import AttentionInterface
+    from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
+
+    AttentionInterface.register(name, decode_attention_forward)
+    AttentionMaskInterface.register(name, sdpa_mask)
+    REGISTERED.add(name)
+    return name

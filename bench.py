@@ -1,0 +1,436 @@
+#!/usr/bin/env python
+"""Benchmark of the sink-cache decode hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...          (one process per GPU)
+
+A step is one layer of one decode step for every stream of this rank: the pending eviction
+of one row with RoPE re-rotation by -1 of every window key (fp32), the append of the new
+token (fp32 K / bf16 V), and GQA decode attention over the n_sink + window + 1 rows -- the
+fused kernel pass of sink_fused_decode_step.  Shapes are one Qwen3-0.6B attention layer
+(16 query heads, 8 KV heads, head_dim 128), n_sink 4, a 32,768-slot cache, 64 streams per
+GPU; the state (12.9 GB per GPU) is far larger than L2, so consecutive steps read HBM.
+
+`value` is the algorithmic bytes of all ranks' steps per second (GB/s) with inputs resident
+in HBM; `e2e` is the same through the public API (SinkLayer.update + the attention backend)
+with each step's q/k/v copied from pinned host memory and its output copied back.
+Streams are independent: ranks split them with no collective on the hot path (weak
+scaling: 64 streams per GPU).  `--impl reference` times the reference's CPU path (the
+oracle port of it) on this host's cores instead.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "decode-step µs/layer & achieved HBM GB/s (attn+evict/rerotate); streamed tok/s at 1/2/4/8 B200"
+HQ, HKV, D, N_SINK = 16, 8, 128, 4
+THETA = 1e6
+L2_BYTES = 126 * 2 ** 20
+FALLBACK_HBM_GBS = 6650.0
+
+
+def alg_bytes(slots: int, n_sink: int = N_SINK, hq: int = HQ, hkv: int = HKV, d: int = D) -> int:
+    """Algorithmic HBM bytes of one layer-step of one stream: every window row read and
+    written once (K fp32 4+4 B, V bf16 2+2 B per element), sink rows read (6 B), the new
+    token read (bf16 k, v) and stored (fp32 k, bf16 v), q read and the output written."""
+    w, e = slots - n_sink, hkv * d
+    return 12 * w * e + 6 * n_sink * e + 10 * e + 4 * hq * d
+
+
+def inv_freq(d: int = D, theta: float = THETA) -> torch.Tensor:
+    return 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+
+
+def hbm_peak() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic() -> dict:
+    """DRAM bytes per launch of the stream kernel from the committed ncu summary, if any
+    (lines `traffic_bytes_per_launch: N` and `traffic_workload: ...`)."""
+    path = os.path.join(ROOT, "profiles", "sink_stream_kernel_traffic.txt")
+    out = {}
+    try:
+        with open(path) as f:
+            for line in f:
+                if ":" in line:
+                    k, v = line.split(":", 1)
+                    out[k.strip()] = v.strip()
+    except OSError:
+        pass
+    return out
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.target = None
+        try:
+            props = torch.cuda.get_device_properties(device)
+            uuid = str(getattr(props, "uuid", "") or "")
+            self.target = uuid if uuid.startswith("GPU-") else (f"GPU-{uuid}" if uuid else None)
+        except Exception:
+            self.target = None
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"]
+        if self.target:
+            cmd += ["-i", self.target]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.15)
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sms, maxes, reasons = [], [], set()
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(self.REASONS, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sms:
+            return None
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ----------------------------------------------------------------------------- workload
+
+
+class OpBench:
+    """One layer of decode state for `batch` streams on one GPU, in the steady state (S + 1
+    rows: S kept, one pending eviction), plus a small pool of per-step inputs."""
+
+    POOL = 4
+
+    def __init__(self, batch: int, slots: int, device: torch.device, seed: int):
+        from attention_sinks_b200 import _lib
+        self.lib = _lib
+        self.batch, self.slots, self.device = batch, slots, device
+        self.window = slots - N_SINK
+        self.scale = D ** -0.5
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.k = torch.empty(batch, HKV, slots + 1, D, dtype=torch.float32, device=device)
+        self.v = torch.empty(batch, HKV, slots + 1, D, dtype=torch.bfloat16, device=device)
+        inv = inv_freq().to(device)
+        freqs = torch.arange(slots + 1, device=device, dtype=torch.float32)[:, None] * inv
+        emb = torch.cat((freqs, freqs), -1)
+        cos_t, sin_t = emb.cos(), emb.sin()
+        for b in range(batch):  # keys ~ N(0,1) rotated at positions 0..S, one stream at a time
+            raw = torch.randn(HKV, slots + 1, D, device=device, generator=g)
+            x1, x2 = raw.chunk(2, -1)
+            self.k[b] = raw * cos_t + torch.cat((-x2, x1), -1) * sin_t
+            self.v[b] = torch.randn(HKV, slots + 1, D, device=device, generator=g).to(torch.bfloat16)
+        del freqs, emb, cos_t, sin_t
+        bf = torch.bfloat16
+        self.q = [torch.randn(batch, HQ, 1, D, device=device, generator=g).to(bf) for _ in range(self.POOL)]
+        self.kn = [torch.randn(batch, HKV, 1, D, device=device, generator=g).to(bf) for _ in range(self.POOL)]
+        self.vn = [torch.randn(batch, HKV, 1, D, device=device, generator=g).to(bf) for _ in range(self.POOL)]
+        cos, sin = torch.cat((-inv.cpu(), -inv.cpu())).cos(), torch.cat((-inv.cpu(), -inv.cpu())).sin()
+        self.cos, self.sin = cos.to(device), sin.to(device)
+        self.out = torch.empty(batch, 1, HQ, D, dtype=bf, device=device)
+        self.ws = _lib.Workspace()
+        sms = _lib.sm_count(device)
+        need = _lib.workspace_bytes(_lib.OP_FUSED_STEP, batch, HKV, HQ, D, torch.float32, bf, slots + 1,
+                                    N_SINK, self.window, 1, sms)
+        self.ws.get(need, device)
+        self.plan = _lib.plan(_lib.OP_FUSED_STEP, batch, HKV, HQ, D, torch.float32, bf, slots + 1,
+                              N_SINK, self.window, 1, sms)
+
+    def launches_per_step(self) -> int:
+        ns = self.plan["splits"]
+        return 1 + (2 if ns > 1 else 0)  # halo pre-pass and split combine when split
+
+    def step(self, i: int) -> None:
+        j = i % self.POOL
+        self.lib.fused_decode_step(self.k, self.v, self.kn[j], self.vn[j], self.q[j], N_SINK, self.window, 1,
+                                   self.slots, self.cos, self.sin, self.scale, self.out, self.ws)
+
+    def state_bytes(self) -> int:
+        return self.k.numel() * 4 + self.v.numel() * 2
+
+
+def time_device(bench: OpBench, steps: int, warmup: int, flush: torch.Tensor | None = None) -> float:
+    """Mean ms per step with CUDA events on the launching stream.  When `flush` is given
+    (state smaller than L2), L2 is overwritten between steps and each step timed alone."""
+    for i in range(warmup):
+        bench.step(i)
+    torch.cuda.synchronize()
+    if flush is None:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(steps):
+            bench.step(i)
+        end.record()
+        end.synchronize()
+        return start.elapsed_time(end) / steps
+    total = 0.0
+    for i in range(steps):
+        flush.fill_(i & 0xFF)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        bench.step(i)
+        end.record()
+        end.synchronize()
+        total += start.elapsed_time(end)
+    return total / steps
+
+
+class _Module:
+    """What the attention backend reads from a Transformers attention module."""
+    training = False
+    num_key_value_groups = HQ // HKV
+    is_causal = True
+
+
+def run_e2e(bench: OpBench, steps: int, warmup: int) -> tuple[float, int, int]:
+    """ms/step through the public API with host buffers: per step the new q/k/v are copied
+    from pinned host memory, SinkLayer.update + the registered attention backend run the
+    fused step, and the output is copied to pinned host memory."""
+    from attention_sinks_b200 import SinkLayer
+    from attention_sinks_b200.decode_attention import decode_attention_forward
+    dev = bench.device
+    layer = SinkLayer(N_SINK, bench.window, inv_freq(), key_dtype=torch.float32, fused=True)
+    chunk = 4096
+    for r0 in range(0, bench.slots + 1, chunk):  # prefill S + 1 rows through update()
+        r1 = min(r0 + chunk, bench.slots + 1)
+        layer.update(bench.k[:, :, r0:r1].to(torch.bfloat16), bench.v[:, :, r0:r1])
+    assert layer.length == bench.slots + 1 and layer._kbuf.shape[-2] == bench.slots + 1
+    pool = OpBench.POOL
+    hq = [bench.q[j].cpu().pin_memory() for j in range(pool)]
+    hk = [bench.kn[j].cpu().pin_memory() for j in range(pool)]
+    hv = [bench.vn[j].cpu().pin_memory() for j in range(pool)]
+    hout = [torch.empty(bench.out.shape, dtype=bench.out.dtype).pin_memory() for _ in range(pool)]
+    module = _Module()
+
+    def step(i):
+        j = i % pool
+        q = hq[j].to(dev, non_blocking=True)
+        k = hk[j].to(dev, non_blocking=True)
+        v = hv[j].to(dev, non_blocking=True)
+        keys, values = layer.update(k, v)
+        o, _ = decode_attention_forward(module, q, keys, values, None, scaling=bench.scale)
+        hout[j].copy_(o, non_blocking=True)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        step(i)
+    end.record()
+    end.synchronize()
+    h2d = (hq[0].numel() + hk[0].numel() + hv[0].numel()) * 2
+    d2h = hout[0].numel() * 2
+    del layer
+    return start.elapsed_time(end) / steps, h2d, d2h
+
+
+def cpu_baseline(slots: int, seconds: float = 15.0) -> dict:
+    """The reference's CPU path (oracle port: SinkLayer.update on the PyTorch branch + SDPA
+    attention) on this host's cores, for one stream of the workload, as many steps as fit
+    in about `seconds`."""
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    layer = oracle.make_prefilled_cache(1, HKV, D, slots, N_SINK, inv_freq(), seed=0)
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, HQ, 1, D, generator=g).bfloat16()
+    kn = torch.randn(1, HKV, 1, D, generator=g).bfloat16()
+    vn = torch.randn(1, HKV, 1, D, generator=g).bfloat16()
+    oracle.reference_cpu_step(layer, q, kn, vn, D ** -0.5)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.reference_cpu_step(layer, q, kn, vn, D ** -0.5)
+        n += 1
+        el = time.perf_counter() - t0
+        if el > seconds or n >= 1000:
+            break
+    ms = el * 1e3 / n
+    return {"value": round(alg_bytes(slots) / (ms * 1e-3) / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port", "ms_per_step": round(ms, 3),
+            "sample": f"1 stream x {slots} slots (of the per-GPU workload), {n} steps, oracle port of "
+                      f"SinkLayer.update (PyTorch path) + SDPA, torch threads={threads}"}
+
+
+def sweep(device: torch.device, flush: torch.Tensor) -> dict:
+    """µs per layer-step and GB/s over the op-bench grid (slots x streams), 1 GPU."""
+    out = {}
+    for slots in (256, 1024, 4096, 32768):
+        for batch in (1, 8, 64):
+            b = OpBench(batch, slots, device, seed=slots + batch)
+            small = b.state_bytes() < 2 * L2_BYTES
+            steps = 50 if small else max(10, min(200, int(2e9 / (alg_bytes(slots) * batch))))
+            ms = time_device(b, steps, 3, flush if small else None)
+            out[f"S{slots}_B{batch}"] = {"us_per_layer": round(ms * 1e3, 2),
+                                        "GB_s": round(alg_bytes(slots) * batch / (ms * 1e-3) / 1e9, 1),
+                                        "l2_flushed": small}
+            del b
+            torch.cuda.empty_cache()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--slots", type=int, default=32768)
+    ap.add_argument("--streams", type=int, default=64, help="streams per GPU")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+
+    from attention_sinks_b200 import streams
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    config = {"workload": f"sink-cache fused decode layer-step: evict 1 + rerotate -1 + append + GQA decode "
+                          f"attention, Qwen3-0.6B layer shape (Hq {HQ}, Hkv {HKV}, head_dim {D})",
+              "slots": args.slots, "n_sink": N_SINK, "window": args.slots - N_SINK,
+              "streams_per_gpu": args.streams, "global_streams": args.streams * max(world_env, 1),
+              "key_dtype": "fp32", "value_dtype": "bf16", "parallelism": f"streams x{max(world_env, 1)} (no collective)",
+              "l2": "state per GPU larger than L2: no flush between steps"}
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        steps = max(1, args.steps)
+        seconds = min(120.0, 0.3 * steps + 5)
+        cb = cpu_baseline(args.slots, seconds=seconds)
+        v = cb["value"] * 1.0
+        line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": config, "cpu_baseline": cb,
+                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    rank, world, local = streams.init_from_env("nccl")
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    from attention_sinks_b200 import build
+    build.build()  # no-op when the shipped library is current
+
+    bench = OpBench(args.streams, args.slots, device, seed=1000 + rank)
+    assert bench.state_bytes() > 2 * L2_BYTES
+    for i in range(args.warmup):
+        bench.step(i)
+    torch.cuda.synchronize()
+    streams.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(device)
+    clocks.start()
+    ms = time_device(bench, args.steps, 0)
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    streams.barrier()
+    ms_max = streams.reduce_max(ms)
+    status = bench.ws.read_status()
+    if status:
+        raise SystemExit(f"kernel status word {status}: a bounded wait ran out")
+
+    e2e_ms, h2d, d2h = run_e2e(bench, args.steps, args.warmup)
+    streams.barrier()
+    e2e_max = streams.reduce_max(e2e_ms)
+
+    bytes_step = alg_bytes(args.slots) * args.streams
+    total_bytes = bytes_step * world
+    value = total_bytes / (ms_max * 1e-3) / 1e9
+    e2e_value = total_bytes / (e2e_max * 1e-3) / 1e9
+    peak, peak_kind = hbm_peak()
+    per_gpu = bytes_step / (ms * 1e-3) / 1e9
+    prof = profiled_traffic()
+    traffic = None
+    if "traffic_bytes_per_launch" in prof:
+        try:
+            traffic = float(prof["traffic_bytes_per_launch"])
+        except ValueError:
+            traffic = None
+    roofline = {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(per_gpu / peak, 4), "traffic": traffic, "peak_source": peak_kind,
+                "kernel": "sink_stream_kernel<float, bf16, 128, 2, true> (timed with its halo pre-pass and "
+                          "split-combine launches: the whole fused step)",
+                "algorithmic_bytes_per_launch": bytes_step}
+    if "traffic_workload" in prof:
+        roofline["traffic_workload"] = prof["traffic_workload"]
+
+    launches = bench.launches_per_step() * args.steps
+    plan = dict(bench.plan)
+    extra = {}
+    if world == 1 and rank == 0:
+        if not args.no_sweep:
+            flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=device)
+            del bench
+            torch.cuda.empty_cache()
+            extra["sweep"] = sweep(device, flush)
+            del flush
+        if not args.no_cpu:
+            extra["cpu_baseline"] = cpu_baseline(args.slots)
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+                "us_per_layer": round(ms_max * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "roofline": roofline,
+                "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_max, 4),
+                        "api": "SinkLayer.update + decode_attention_forward (fused step)"},
+                "gpu_launches": launches, "clocks": clk, "plan": plan}
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+    streams.shutdown()
+
+
+if __name__ == "__main__":
+    main()

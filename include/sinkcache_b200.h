@@ -1,0 +1,181 @@
+/*
+ * sinkcache_b200.h -- C ABI of the B200 (sm_100a) attention-sink KV-cache decode path.
+ *
+ * The library replaces the GPU work of the sinkcache package (buttaRahul/Attention_sinks):
+ *   - the per-layer append of new K/V rows     (src/sinkcache/cache.py:159-160)
+ *   - the in-place eviction + RoPE re-rotation (src/sinkcache/kernels.py:24-73, cache.py:129-147)
+ *   - split-K GQA decode attention             (src/sinkcache/decode_attention.py:29-130)
+ *   - and a fused decode step doing all three in one pass over the cache.
+ *
+ * Conventions
+ *   - Every tensor is described by plain pointers, sizes and element strides.  The last
+ *     dimension (head_dim) is always contiguous.  Cache buffers additionally need their
+ *     rows (slots) contiguous: stride between slots == head_dim.
+ *   - Cache buffers are [batch, heads_kv, slots, head_dim] (the layout SinkLayer._alloc
+ *     creates, cache.py:97-104): K in k_dtype (float32 by default), V in the model dtype.
+ *   - All launches go to `stream` (a cudaStream_t passed as void*); nothing synchronises,
+ *     nothing allocates.  Scratch memory ("workspace") is owned by the caller; its size
+ *     comes from sink_workspace_bytes().  Every launch is CUDA-graph capturable.
+ *   - Return value: 0 on success, a negative SINK_E* code for a rejected argument, or a
+ *     positive cudaError_t from the launch.  sink_strerror() describes any code.
+ *   - The device workspace starts with a 32-bit status word.  A kernel whose bounded wait
+ *     for a bulk copy runs out sets a SINK_STATUS_* bit there instead of hanging;
+ *     sink_read_status() returns and clears it.
+ */
+#ifndef SINKCACHE_B200_H
+#define SINKCACHE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SINK_ABI_VERSION 1
+
+/* element types */
+#define SINK_DTYPE_F32 0
+#define SINK_DTYPE_BF16 1
+#define SINK_DTYPE_F16 2
+
+/* argument errors (negative return codes) */
+#define SINK_OK 0
+#define SINK_EINVAL (-1)      /* a size or index out of range */
+#define SINK_EDTYPE (-2)      /* unsupported dtype combination */
+#define SINK_EHEADDIM (-3)    /* head_dim not in {64, 128, 256} */
+#define SINK_EGROUP (-4)      /* heads_q / heads_kv not an integer in [1, 8] */
+#define SINK_ELAYOUT (-5)     /* slots not contiguous, or a pointer not 16-byte aligned */
+#define SINK_EWORKSPACE (-6)  /* workspace missing or smaller than sink_workspace_bytes() */
+#define SINK_EDEVICE (-7)     /* no usable CUDA device */
+
+/* status bits written by kernels into the workspace status word */
+#define SINK_STATUS_WAIT_TIMEOUT 1
+
+/* operations, for sink_workspace_bytes() */
+#define SINK_OP_APPEND 0
+#define SINK_OP_EVICT 1
+#define SINK_OP_ATTEND 2
+#define SINK_OP_FUSED_STEP 3
+
+/* One layer's K/V cache buffers: [batch, heads_kv, slots, head_dim] each. */
+typedef struct sink_kv_buffers {
+  void* k;
+  void* v;
+  int32_t k_dtype;
+  int32_t v_dtype;
+  int32_t batch;
+  int32_t heads_kv;
+  int32_t slots;     /* allocated rows per (batch, head) */
+  int32_t head_dim;
+  int64_t k_stride_b; /* element strides of the batch and head dimensions */
+  int64_t k_stride_h;
+  int64_t v_stride_b;
+  int64_t v_stride_h;
+} sink_kv_buffers_t;
+
+/* A [batch, heads, n, head_dim] tensor with a unit last stride (k/v of a new chunk, q, out). */
+typedef struct sink_rows {
+  void* data;
+  int32_t dtype;
+  int32_t heads;
+  int32_t n;
+  int32_t pad_;
+  int64_t stride_b;
+  int64_t stride_h;
+  int64_t stride_t;
+} sink_rows_t;
+
+/* Library ABI version (SINK_ABI_VERSION). */
+int32_t sink_abi_version(void);
+
+/* Human-readable text for any return code of this library (negative or cudaError_t). */
+const char* sink_strerror(int32_t code);
+
+/*
+ * Bytes of device workspace that `op` needs for these shapes (0 if none).  `num_sms` is the
+ * device's multiprocessor count (cudaDevAttrMultiProcessorCount); the launch uses the same
+ * count, so size the workspace for the device it will run on.  `rows` is the number of
+ * attended cache rows for SINK_OP_ATTEND and SINK_OP_FUSED_STEP (after the append).
+ * Pure host arithmetic: callable without a GPU.
+ */
+size_t sink_workspace_bytes(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q,
+                            int32_t head_dim, int32_t k_dtype, int32_t v_dtype, int32_t rows,
+                            int32_t n_sink, int32_t window, int32_t drop, int32_t num_sms);
+
+/*
+ * Split plan the launch will use (for tests and profiling): number of splits per
+ * (batch, head) pair, rows per split, rows per pipeline chunk, pipeline stages and
+ * dynamic shared memory per CTA.  Pure host arithmetic.  Returns 0 or SINK_E*.
+ */
+int32_t sink_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, int32_t head_dim,
+                  int32_t k_dtype, int32_t v_dtype, int32_t rows, int32_t n_sink, int32_t window,
+                  int32_t drop, int32_t num_sms, int32_t* splits, int32_t* rows_per_split,
+                  int32_t* chunk_rows, int32_t* stages, int32_t* smem_bytes);
+
+/*
+ * Append: kv[:, :, row:row+n] = (k_new, v_new)  (k converted to k_dtype exactly, or rounded
+ * to nearest-even when k_dtype is narrower).
+ * Replaces SinkLayer.update's `self._kbuf[:, :, self.length:end].copy_(key_states)` and the
+ * matching V copy (cache.py:159-160).  k_new/v_new: model dtype == kv->v_dtype, n rows.
+ */
+int32_t sink_append(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
+                    const sink_rows_t* v_new, int32_t row, void* stream);
+
+/*
+ * Eviction with re-rotation, in place, for every (batch, head):
+ *   K[s : s+W] = rope(K[s+drop : s+drop+W], -drop)   (fp32 math, one rounding to k_dtype)
+ *   V[s : s+W] = V[s+drop : s+drop+W]
+ * with s = n_sink, W = window.  cos/sin are the float32 [head_dim] tables for the angle -drop
+ * (rope_cos_sin(-drop, inv_freq), HF half-split layout, both halves equal); ignored when
+ * rotate == 0 (shift only: the rerotate_keys=False ablation).  Rows [0, s) are untouched.
+ * Needs s + W + drop <= slots.  drop == 0 is a no-op.
+ * Replaces shift_window_ (kernels.py:59-73) as called by SinkLayer._evict_pending
+ * (cache.py:134-137), and the PyTorch branch of the same method (cache.py:138-143).
+ */
+int32_t sink_evict_rerotate(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t window,
+                            int32_t drop, const float* cos_tab, const float* sin_tab,
+                            int32_t rotate, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/*
+ * Decode attention for one query token per sequence over the first `rows` cache rows:
+ *   out[b, 0, hq, :] = softmax(q[b, hq] . K[b, hq / G, :rows]^T * scale) @ V[b, hq / G, :rows]
+ * with G = q->heads / heads_kv (grouped-query attention, HF repeat_kv head order).
+ * q: [batch, heads_q, 1, head_dim] in the model dtype; out: [batch, 1, heads_q, head_dim]
+ * in the model dtype, given by pointer and its batch / head element strides.
+ * K may be float32 (read directly, no bf16 copy) or the model dtype.
+ * Replaces flash_decode (decode_attention.py:102-130): split-K partials + a combine pass.
+ */
+int32_t sink_decode_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows,
+                              float scale, void* out, int64_t out_stride_b,
+                              int64_t out_stride_h, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/*
+ * One fused decode step of a sink layer, q_len == 1:
+ *   1. pending eviction of `drop` rows with re-rotation (as sink_evict_rerotate; drop may be 0)
+ *   2. append of (k_new, v_new) at row `append_row` (== n_sink + window when drop > 0)
+ *   3. decode attention of q over rows [0, append_row] of the updated cache
+ * in one pass over the cache: every window row is read once, re-rotated in registers,
+ * written back once and consumed by the attention in the same CTA.
+ * Replaces SinkLayer.update (cache.py:151-165) followed by decode_attention_forward
+ * (decode_attention.py:136-143) for a one-token step; the cache contents afterwards are
+ * those SinkLayer.update leaves, without the bf16 key copy of cache.py:163.
+ */
+int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
+                               const sink_rows_t* v_new, const sink_rows_t* q,
+                               int32_t n_sink, int32_t window, int32_t drop,
+                               int32_t append_row, const float* cos_tab, const float* sin_tab,
+                               int32_t rotate, float scale, void* out, int64_t out_stride_b,
+                               int64_t out_stride_h, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/* Copy the workspace status word to *status (synchronises `stream`) and clear it. */
+int32_t sink_read_status(void* workspace, void* stream, int32_t* status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SINKCACHE_B200_H */

@@ -1,0 +1,99 @@
+"""The C ABI library: it loads, exports every entry point include/*.h declares, and its
+host-only functions (planning, workspace sizing, argument checks) behave -- no GPU needed."""
+
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+import torch
+
+from attention_sinks_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = []
+    for header in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(header).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names += re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(sink_\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol(built_lib):
+    names = declared_functions()
+    assert len(names) >= 9, names
+    for name in names:
+        assert hasattr(built_lib, name), f"{name} declared in include/ but not exported"
+    assert set(_lib.EXPORTED_SYMBOLS) <= set(names)
+
+
+def test_abi_version_and_errors(built_lib):
+    assert built_lib.sink_abi_version() == 1
+    for code in (0, -1, -2, -3, -4, -5, -6, -7):
+        assert _lib.strerror(code)
+    assert "sinkcache_b200" in _lib.strerror(-6)
+
+
+def test_workspace_and_plan_are_host_arithmetic(built_lib):
+    f32, bf16 = torch.float32, torch.bfloat16
+    # op bench at 32,768 slots, 8 streams, Qwen3 layer shape
+    p = _lib.plan(_lib.OP_FUSED_STEP, 8, 8, 16, 128, f32, bf16, 32769, 4, 32764, 1, 148)
+    assert p["chunk_rows"] == 32 and p["stages"] == 4
+    assert p["smem_bytes"] * 2 <= 233472  # two CTAs per SM
+    assert p["splits"] * p["rows_per_split"] >= 32769 > (p["splits"] - 1) * p["rows_per_split"]
+    ws = _lib.workspace_bytes(_lib.OP_FUSED_STEP, 8, 8, 16, 128, f32, bf16, 32769, 4, 32764, 1, 148)
+    assert ws >= 256
+    # unsupported shapes are rejected with 0 bytes / an error code
+    assert built_lib.sink_workspace_bytes(_lib.OP_ATTEND, 1, 8, 16, 96, 0, 1, 10, 0, 1, 0, 148) == 0
+    assert built_lib.sink_workspace_bytes(_lib.OP_ATTEND, 1, 8, 12, 128, 0, 1, 10, 0, 1, 0, 148) == 0
+    assert built_lib.sink_workspace_bytes(_lib.OP_ATTEND, 1, 1, 16, 128, 0, 1, 10, 0, 1, 0, 148) == 0
+    _lib.plan(_lib.OP_EVICT, 1, 8, 8, 128, f32, torch.float16, 0, 4, 60, 1, 148)  # fp32 K, fp16 V
+    with pytest.raises(RuntimeError):
+        _lib.plan(_lib.OP_EVICT, 1, 8, 8, 128, torch.float16, bf16, 0, 4, 60, 1, 148)  # mixed 16-bit
+
+
+@pytest.mark.parametrize("op,rows,n_sink,window,drop", [
+    (_lib.OP_EVICT, 0, 4, 60, 1), (_lib.OP_EVICT, 0, 4, 32764, 1), (_lib.OP_EVICT, 0, 2, 7, 200),
+    (_lib.OP_ATTEND, 1, 0, 1, 0), (_lib.OP_ATTEND, 4097, 0, 1, 0), (_lib.OP_FUSED_STEP, 1025, 4, 1020, 1),
+    (_lib.OP_FUSED_STEP, 257, 4, 252, 0),
+])
+@pytest.mark.parametrize("batch", [1, 8, 64])
+def test_plan_covers_rows_exactly(op, rows, n_sink, window, drop, batch):
+    """Splits tile the rows with no gap and no empty split; halo rows fit their region."""
+    p = _lib.plan(op, batch, 8, 16, 128, torch.float32, torch.bfloat16, rows, n_sink, window, drop, 148)
+    total = window if op == _lib.OP_EVICT else rows
+    ns, rps, t = p["splits"], p["rows_per_split"], p["chunk_rows"]
+    assert rps % t == 0 and 1 <= ns <= 256
+    assert (ns - 1) * rps < total <= ns * rps
+
+
+def test_argument_errors_return_codes_without_a_gpu(built_lib):
+    """Rejected arguments come back as codes; nothing is launched."""
+    kv = _lib.KVBuffers()  # null pointers
+    rows = _lib.Rows()
+    assert built_lib.sink_append(ctypes.byref(kv), ctypes.byref(rows), ctypes.byref(rows), 0, None) == -1
+    assert built_lib.sink_evict_rerotate(ctypes.byref(kv), 4, 60, 1, None, None, 1, None, 0, None) == -1
+    kv = _lib.KVBuffers(16, 32, 0, 1, 1, 8, 65, 96, 65 * 96 * 8, 65 * 96, 65 * 96 * 8, 65 * 96)
+    assert built_lib.sink_evict_rerotate(ctypes.byref(kv), 4, 60, 1, None, None, 0, None, 0, None) == -3
+    kv = _lib.KVBuffers(16, 32, 2, 1, 1, 8, 65, 128, 65 * 128 * 8, 65 * 128, 65 * 128 * 8, 65 * 128)
+    assert built_lib.sink_evict_rerotate(ctypes.byref(kv), 4, 60, 1, None, None, 0, None, 0, None) == -2
+    kv = _lib.KVBuffers(8, 32, 0, 1, 1, 8, 65, 128, 65 * 128 * 8, 65 * 128, 65 * 128 * 8, 65 * 128)
+    assert built_lib.sink_evict_rerotate(ctypes.byref(kv), 4, 60, 1, None, None, 0, None, 0, None) == -5
+    kv = _lib.KVBuffers(16, 32, 0, 1, 1, 8, 65, 128, 65 * 128 * 8, 65 * 128, 65 * 128 * 8, 65 * 128)
+    assert built_lib.sink_evict_rerotate(ctypes.byref(kv), 4, 61, 1, None, None, 0, None, 0, None) == -1
+    assert built_lib.sink_evict_rerotate(ctypes.byref(kv), 4, 60, 0, None, None, 0, None, 0, None) == 0
+
+
+def test_product_refuses_cpu_tensors():
+    """No CPU path: the kernels' wrappers reject host tensors instead of computing."""
+    k = torch.zeros(1, 8, 65, 128)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _lib.kv_desc(k, k.bfloat16())
+    from attention_sinks_b200 import SinkLayer
+    layer = SinkLayer(4, 60, torch.ones(64))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        layer.update(torch.zeros(1, 8, 1, 128, dtype=torch.bfloat16), torch.zeros(1, 8, 1, 128, dtype=torch.bfloat16))
