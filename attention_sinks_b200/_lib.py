@@ -62,9 +62,9 @@ def _declare(lib):
         "sink_plan": (i32, [i32] * 12 + [pi32] * 5),
         "sink_append": (i32, [pkv, prows, prows, i32, vp]),
         "sink_evict_rerotate": (i32, [pkv, i32, i32, i32, fp, fp, i32, vp, sz, vp]),
-        "sink_decode_attention": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, i64, vp, sz, vp]),
+        "sink_decode_attention": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
         "sink_fused_decode_step": (i32, [pkv, prows, prows, prows, i32, i32, i32, i32, fp, fp, i32,
-                                         ctypes.c_float, vp, i64, i64, vp, sz, vp]),
+                                         ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
         "sink_read_status": (i32, [vp, vp, pi32]),
     }
     for name, (res, args) in sig.items():
@@ -226,17 +226,33 @@ def evict_rerotate(kbuf: torch.Tensor, vbuf: torch.Tensor, n_sink: int, window: 
     _check(rc, "sink_evict_rerotate")
 
 
+def mask_arg(mask: torch.Tensor | None, batch: int, rows: int) -> tuple[int | None, int]:
+    """(pointer, batch stride in bytes) of a boolean [B or 1, 1, 1, rows] attention mask for
+    a one-token query (True = attend), as the kernels take it."""
+    if mask is None:
+        return None, 0
+    if (mask.dtype != torch.bool or mask.dim() != 4 or mask.shape[1] != 1 or mask.shape[2] != 1
+            or mask.shape[3] != rows or mask.shape[0] not in (1, batch)):
+        raise ValueError(f"kernel masks are boolean [B, 1, 1, {rows}], got {mask.dtype} {tuple(mask.shape)}")
+    _require_cuda(mask)
+    if mask.stride(-1) != 1:
+        mask = mask.contiguous()
+    return mask.data_ptr(), (mask.stride(0) if mask.shape[0] > 1 else 0)
+
+
 def decode_attention(q: torch.Tensor, kbuf: torch.Tensor, vbuf: torch.Tensor, rows: int, scale: float,
-                     out: torch.Tensor, ws: Workspace) -> torch.Tensor:
-    """out[B, 1, Hq, D] = attention of q[B, Hq, 1, D] over kbuf/vbuf rows [0, rows)."""
+                     out: torch.Tensor, ws: Workspace, mask: torch.Tensor | None = None) -> torch.Tensor:
+    """out[B, 1, Hq, D] = attention of q[B, Hq, 1, D] over kbuf/vbuf rows [0, rows), rows
+    with a False `mask` entry left out."""
     kv = kv_desc(kbuf, vbuf)
     b, h, _, d = kbuf.shape
     need = workspace_bytes(OP_ATTEND, b, h, q.shape[1], d, kbuf.dtype, vbuf.dtype, rows, 0, 1, 0,
                            sm_count(kbuf.device))
     buf = ws.get(need, kbuf.device)
+    mptr, msb = mask_arg(mask, b, rows)
     rc = lib().sink_decode_attention(ctypes.byref(rows_desc(q)), ctypes.byref(kv), int(rows), float(scale),
-                                     out.data_ptr(), out.stride(0), out.stride(2), buf.data_ptr(), buf.numel(),
-                                     stream_handle(kbuf.device))
+                                     mptr, msb, out.data_ptr(), out.stride(0), out.stride(2), buf.data_ptr(),
+                                     buf.numel(), stream_handle(kbuf.device))
     _check(rc, "sink_decode_attention")
     return out
 
@@ -244,7 +260,7 @@ def decode_attention(q: torch.Tensor, kbuf: torch.Tensor, vbuf: torch.Tensor, ro
 def fused_decode_step(kbuf: torch.Tensor, vbuf: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                       q: torch.Tensor, n_sink: int, window: int, drop: int, append_row: int,
                       cos: torch.Tensor | None, sin: torch.Tensor | None, scale: float,
-                      out: torch.Tensor, ws: Workspace) -> torch.Tensor:
+                      out: torch.Tensor, ws: Workspace, mask: torch.Tensor | None = None) -> torch.Tensor:
     """Evict `drop` rows (re-rotating keys), append (k, v) at `append_row`, attend q over rows
     [0, append_row] -- one pass over the cache."""
     kv = kv_desc(kbuf, vbuf)
@@ -253,10 +269,11 @@ def fused_decode_step(kbuf: torch.Tensor, vbuf: torch.Tensor, k: torch.Tensor, v
                            n_sink, window, drop, sm_count(kbuf.device))
     buf = ws.get(need, kbuf.device)
     rotate = cos is not None
+    mptr, msb = mask_arg(mask, b, append_row + 1)
     rc = lib().sink_fused_decode_step(
         ctypes.byref(kv), ctypes.byref(rows_desc(k)), ctypes.byref(rows_desc(v)), ctypes.byref(rows_desc(q)),
         n_sink, window, drop, append_row, cos.data_ptr() if rotate else None,
-        sin.data_ptr() if rotate else None, 1 if rotate else 0, float(scale), out.data_ptr(),
+        sin.data_ptr() if rotate else None, 1 if rotate else 0, float(scale), mptr, msb, out.data_ptr(),
         out.stride(0), out.stride(2), buf.data_ptr(), buf.numel(), stream_handle(kbuf.device))
     _check(rc, "sink_fused_decode_step")
     return out

@@ -174,15 +174,16 @@ class SinkLayer(CacheLayerMixin):
         self.keys, self.values = keys, self._vbuf[:, :, :end]
         return self.keys, self.values
 
-    def run_pending(self, query: torch.Tensor, scale: float) -> torch.Tensor:
-        """Run the deferred step fused with its attention; returns [B, 1, Hq, D]."""
+    def run_pending(self, query: torch.Tensor, scale: float, mask: torch.Tensor | None = None) -> torch.Tensor:
+        """Run the deferred step fused with its attention; returns [B, 1, Hq, D].  `mask`:
+        optional boolean [B, 1, 1, rows] (rows left out of the attention where False)."""
         drop, k, v, row = self._pending
         self._pending = None
         cos, sin = self._rotation(drop) if (drop > 0 and self.rerotate_keys) else (None, None)
         b, hq, _, d = query.shape
         out = torch.empty(b, 1, hq, d, dtype=query.dtype, device=query.device)
         return _lib.fused_decode_step(self._kbuf, self._vbuf, k, v, query, self.n_sink, self.window,
-                                      drop, row, cos, sin, scale, out, self._ws)
+                                      drop, row, cos, sin, scale, out, self._ws, mask)
 
     def materialize(self) -> None:
         """Apply a deferred step (eviction + append) without its attention."""

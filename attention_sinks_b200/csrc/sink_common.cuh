@@ -47,6 +47,8 @@ struct StreamArgs {
   int row_begin, row_end, append_row, written_end;
   int ns, rows_per_split, halo_rows;
   float scale_log2;
+  const uint8_t* mask;  // optional [batch] x row_end booleans: attend to row r iff nonzero
+  int64_t mask_sb;      // batch stride of the mask in bytes (0: one row shared by the batch)
   float* o_part;
   float* m_part;
   float* l_part;

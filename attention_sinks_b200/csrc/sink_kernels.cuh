@@ -135,6 +135,7 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
       sn[i] = A.sin_tab[4 * li + i];
     }
   }
+  const uint8_t* mrow = A.mask != nullptr ? A.mask + b * A.mask_sb : nullptr;
   float qlo[ATTEND ? GMAX : 1][4], qhi[ATTEND ? GMAX : 1][4];
   float m[ATTEND ? GMAX : 1], l[ATTEND ? GMAX : 1], acc[ATTEND ? GMAX : 1][8];
   if constexpr (ATTEND) {
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
         Elem<KT>::store4(krow + D / 2 + 4 * li, hi);
       }
       if constexpr (ATTEND) {
+        const bool seen = valid && (mrow == nullptr || mrow[r] != 0);
 #pragma unroll
         for (int g = 0; g < GMAX; ++g) {
           float d = 0.f;
@@ -215,7 +217,7 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
           for (int k = 0; k < 4; ++k) d = __fmaf_rn(qhi[g][k], hi[k], d);
 #pragma unroll
           for (int off = LPR / 2; off >= 1; off >>= 1) d += __shfl_xor_sync(kFull, d, off);
-          sc[g][i] = valid ? d : NEG_INF;
+          sc[g][i] = seen ? d : NEG_INF;
         }
       }
     }

@@ -396,9 +396,9 @@ int32_t sink_evict_rerotate(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t
 }
 
 int32_t sink_decode_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows,
-                              float scale, void* out, int64_t out_stride_b,
-                              int64_t out_stride_h, void* workspace, size_t workspace_bytes,
-                              void* stream) {
+                              float scale, const uint8_t* mask, int64_t mask_stride_b,
+                              void* out, int64_t out_stride_b, int64_t out_stride_h,
+                              void* workspace, size_t workspace_bytes, void* stream) {
   int32_t rc = check_kv(kv);
   if (rc) return rc;
   if (!q || !q->data || !out) return SINK_EINVAL;
@@ -426,6 +426,8 @@ int32_t sink_decode_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv,
   A.row_end = rows;
   A.written_end = 0;
   A.scale_log2 = scale * kLog2e;
+  A.mask = mask;
+  A.mask_sb = mask_stride_b;
   const int pairs = kv->batch * kv->heads_kv;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((rc = dispatch_stream<true>(kv->k_dtype, kv->v_dtype, kv->head_dim, A.group, A, pl, pairs, st, dev)))
@@ -438,7 +440,8 @@ int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k
                                const sink_rows_t* v_new, const sink_rows_t* q,
                                int32_t n_sink, int32_t window, int32_t drop,
                                int32_t append_row, const float* cos_tab, const float* sin_tab,
-                               int32_t rotate, float scale, void* out, int64_t out_stride_b,
+                               int32_t rotate, float scale, const uint8_t* mask,
+                               int64_t mask_stride_b, void* out, int64_t out_stride_b,
                                int64_t out_stride_h, void* workspace, size_t workspace_bytes,
                                void* stream) {
   int32_t rc = check_kv(kv);
@@ -489,6 +492,8 @@ int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k
   A.append_row = append_row;
   A.written_end = drop > 0 ? n_sink + window + 1 : append_row + 1;
   A.scale_log2 = scale * kLog2e;
+  A.mask = mask;
+  A.mask_sb = mask_stride_b;
   const int pairs = kv->batch * kv->heads_kv;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((rc = launch_halo(kv, A, pl, pairs, st))) return rc;

@@ -8,9 +8,9 @@ kernel merges the splits.  Keys may be float32 (the sink cache's storage, read d
 no bf16 copy of the cache per step) or the model dtype.
 
 `register(name)` (decode_attention.py:149-156) installs `decode_attention_forward` as a
-Transformers attention backend: one-token steps without a mask run on the kernels --
-fused with the cache update when the key view comes from a deferred SinkLayer step --
-and anything else (prefill chunks, masks) falls back to SDPA, as the reference does.
+Transformers attention backend: one-token steps run on the kernels -- fused with the cache
+update when the key view comes from a deferred SinkLayer step -- with no mask or a boolean
+one; multi-token chunks (prefill) and other masks fall back to SDPA, as in the reference.
 """
 
 import torch
@@ -22,16 +22,32 @@ REGISTERED: set[str] = set()
 calls = {"decode_kernel": 0, "fused_step": 0, "sdpa_fallback": 0}
 
 
-def flash_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
+def flash_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                 mask: torch.Tensor | None = None) -> torch.Tensor:
     """q [B, Hq, 1, D]; k, v [B, Hkv, L, D] with contiguous rows (views of a larger cache
-    buffer are fine).  Returns the attention output as [B, 1, Hq, D] in q's dtype."""
+    buffer are fine).  Returns the attention output as [B, 1, Hq, D] in q's dtype.
+    `mask`: optional boolean [B or 1, 1, 1, L], True = attend."""
     bsz, hq, q_len, dim = q.shape
     if q_len != 1 or hq % k.shape[1]:
         raise ValueError(f"flash_decode needs one query token and Hq % Hkv == 0, got q {tuple(q.shape)}, "
                          f"k {tuple(k.shape)}")
     out = torch.empty(bsz, 1, hq, dim, device=q.device, dtype=q.dtype)
     ws = _lib.Workspace()  # per call, like the reference's partials: safe under graph capture
-    return _lib.decode_attention(q, k, v, k.shape[2], scale, out, ws)
+    return _lib.decode_attention(q, k, v, k.shape[2], scale, out, ws, mask)
+
+
+def _on_kernel_device(query: torch.Tensor) -> bool:
+    return query.is_cuda
+
+
+def _kernel_mask_ok(mask, query: torch.Tensor, key: torch.Tensor) -> bool:
+    """The kernels take no mask or a boolean [B or 1, 1, 1, L] one.  Transformers skips the
+    mask of an unpadded one-token step, except while a CUDA graph is being captured, when it
+    passes the all-True boolean mask instead; padded batches pass a boolean mask too."""
+    if mask is None:
+        return True
+    return (mask.dtype == torch.bool and mask.dim() == 4 and mask.shape[1] == 1 and mask.shape[2] == 1
+            and mask.shape[3] == key.shape[-2] and mask.shape[0] in (1, query.shape[0]))
 
 
 def decode_attention_forward(module, query, key, value, attention_mask, dropout=0.0, scaling=None, **kwargs):
@@ -40,13 +56,14 @@ def decode_attention_forward(module, query, key, value, attention_mask, dropout=
     from transformers.integrations.sdpa_attention import sdpa_attention_forward
 
     layer = pending_layer(key)
-    if query.shape[2] == 1 and attention_mask is None and query.is_cuda and not module.training:
+    if (query.shape[2] == 1 and _on_kernel_device(query) and not module.training
+            and _kernel_mask_ok(attention_mask, query, key)):
         scale = scaling if scaling is not None else query.shape[-1] ** -0.5
         if layer is not None:
             calls["fused_step"] += 1
-            return layer.run_pending(query, scale), None
+            return layer.run_pending(query, scale, attention_mask), None
         calls["decode_kernel"] += 1
-        return flash_decode(query, key, value, scale), None
+        return flash_decode(query, key, value, scale, attention_mask), None
     if layer is not None:
         layer.materialize()
     calls["sdpa_fallback"] += 1

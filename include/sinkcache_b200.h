@@ -145,12 +145,15 @@ int32_t sink_evict_rerotate(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t
  * q: [batch, heads_q, 1, head_dim] in the model dtype; out: [batch, 1, heads_q, head_dim]
  * in the model dtype, given by pointer and its batch / head element strides.
  * K may be float32 (read directly, no bf16 copy) or the model dtype.
+ * `mask` (optional, may be NULL): one byte per (batch, row), row r attended iff nonzero,
+ * rows contiguous, batch stride `mask_stride_b` bytes (0 to share one row across the batch)
+ * -- the boolean [B, 1, 1, rows] mask an SDPA-style backend receives for a one-token query.
  * Replaces flash_decode (decode_attention.py:102-130): split-K partials + a combine pass.
  */
 int32_t sink_decode_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows,
-                              float scale, void* out, int64_t out_stride_b,
-                              int64_t out_stride_h, void* workspace, size_t workspace_bytes,
-                              void* stream);
+                              float scale, const uint8_t* mask, int64_t mask_stride_b,
+                              void* out, int64_t out_stride_b, int64_t out_stride_h,
+                              void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * One fused decode step of a sink layer, q_len == 1:
@@ -158,7 +161,9 @@ int32_t sink_decode_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv,
  *   2. append of (k_new, v_new) at row `append_row` (== n_sink + window when drop > 0)
  *   3. decode attention of q over rows [0, append_row] of the updated cache
  * in one pass over the cache: every window row is read once, re-rotated in registers,
- * written back once and consumed by the attention in the same CTA.
+ * written back once and consumed by the attention in the same CTA.  `mask` as for
+ * sink_decode_attention, over rows [0, append_row] (masked rows are still evicted and
+ * re-rotated; they only drop out of the attention).
  * Replaces SinkLayer.update (cache.py:151-165) followed by decode_attention_forward
  * (decode_attention.py:136-143) for a one-token step; the cache contents afterwards are
  * those SinkLayer.update leaves, without the bf16 key copy of cache.py:163.
@@ -167,7 +172,8 @@ int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k
                                const sink_rows_t* v_new, const sink_rows_t* q,
                                int32_t n_sink, int32_t window, int32_t drop,
                                int32_t append_row, const float* cos_tab, const float* sin_tab,
-                               int32_t rotate, float scale, void* out, int64_t out_stride_b,
+                               int32_t rotate, float scale, const uint8_t* mask,
+                               int64_t mask_stride_b, void* out, int64_t out_stride_b,
                                int64_t out_stride_h, void* workspace, size_t workspace_bytes,
                                void* stream);
 

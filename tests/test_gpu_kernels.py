@@ -197,7 +197,7 @@ def test_fused_stream_matches_oracle(batch, hq, hkv, d, n_sink, window, steps, b
             torch.testing.assert_close(out.float().cpu(), want_out, rtol=2e-2, atol=1e-2)
             torch.testing.assert_close(vbuf[:, :, :length].cpu(), want.vbuf[:, :, :length], rtol=0, atol=0)
             assert digest(kbuf[:, :, :length].cpu()) == digest(want.kbuf[:, :, :length])
-    assert length == cap + 1 and want.tokens_evicted == steps + cap + prefill - cap
+    assert length == cap + 1 and want.tokens_evicted == prefill + steps + cap - (cap + 1)
     _status_clean(ws)
 
 
@@ -226,3 +226,57 @@ def test_fused_equals_unfused(built_lib):
     torch.testing.assert_close(ka, kb, rtol=0, atol=0)
     torch.testing.assert_close(va, vb, rtol=0, atol=0)
     torch.testing.assert_close(oa, ob, rtol=0, atol=0)
+
+
+def _masked_oracle(q, k, v, mask, scale):
+    """Attention per stream over the rows its boolean mask keeps."""
+    outs = []
+    for b in range(q.shape[0]):
+        keep = mask[min(b, mask.shape[0] - 1), 0, 0]
+        outs.append(oracle.decode_attention(q[b:b + 1], k[b:b + 1, :, keep], v[b:b + 1, :, keep], scale))
+    return torch.cat(outs, 0)
+
+
+@pytest.mark.parametrize("mask_batch", [1, 3])
+def test_decode_attention_with_boolean_mask(mask_batch, built_lib):
+    """A padded batch's boolean [B, 1, 1, L] mask: masked rows get no weight."""
+    g = torch.Generator().manual_seed(21)
+    b, hq, hkv, d, rows = 3, 16, 8, 128, 2100
+    q = torch.randn(b, hq, 1, d, generator=g).bfloat16()
+    k = torch.randn(b, hkv, rows, d, generator=g) * 3
+    v = torch.randn(b, hkv, rows, d, generator=g).bfloat16()
+    mask = torch.rand(mask_batch, 1, 1, rows, generator=g) > 0.3
+    mask[..., 0] = True
+    out = torch.empty(b, 1, hq, d, dtype=torch.bfloat16, device=DEV)
+    _lib.decode_attention(q.to(DEV), k.to(DEV), v.to(DEV), rows, d ** -0.5, out, _lib.Workspace(), mask.to(DEV))
+    want = _masked_oracle(q, k, v, mask, d ** -0.5)
+    torch.testing.assert_close(out.float().cpu(), want, rtol=2e-2, atol=1e-2)
+    # an all-True mask gives exactly the unmasked result (what graph capture passes)
+    ones = torch.ones(1, 1, 1, rows, dtype=torch.bool, device=DEV)
+    o1, o2 = torch.empty_like(out), torch.empty_like(out)
+    _lib.decode_attention(q.to(DEV), k.to(DEV), v.to(DEV), rows, d ** -0.5, o1, _lib.Workspace(), ones)
+    _lib.decode_attention(q.to(DEV), k.to(DEV), v.to(DEV), rows, d ** -0.5, o2, _lib.Workspace())
+    torch.testing.assert_close(o1, o2, rtol=0, atol=0)
+
+
+def test_fused_step_with_boolean_mask(built_lib):
+    """Masked rows are still evicted and re-rotated; they only leave the attention."""
+    spec = dict(batch=2, hq=16, hkv=8, d=128, slots=300, n_sink=4)
+    st = cases.step_inputs(**spec)
+    n_sink, slots = spec["n_sink"], spec["slots"]
+    want = oracle.OracleSinkLayer(n_sink, slots - n_sink, st["inv"])
+    want.update(st["k0"], st["v0"])
+    keys, values = want.update(st["k1"], st["v1"])
+    g = torch.Generator().manual_seed(2)
+    mask = torch.rand(2, 1, 1, slots + 1, generator=g) > 0.5
+    mask[..., -1] = True
+    want_out = _masked_oracle(st["q"], keys, values, mask, spec["d"] ** -0.5)
+    kbuf, vbuf = st["k0"].float().to(DEV), st["v0"].to(DEV)
+    cos, sin = [t.to(DEV) for t in oracle.rope_cos_sin(torch.tensor(-1), st["inv"])]
+    out = torch.empty(2, 1, 16, 128, dtype=torch.bfloat16, device=DEV)
+    _lib.fused_decode_step(kbuf, vbuf, st["k1"].to(DEV), st["v1"].to(DEV), st["q"].to(DEV), n_sink,
+                           slots - n_sink, 1, slots, cos, sin, spec["d"] ** -0.5, out, _lib.Workspace(),
+                           mask.to(DEV))
+    assert digest(kbuf.cpu()) == digest(want.kbuf)
+    torch.testing.assert_close(vbuf.cpu(), want.vbuf, rtol=0, atol=0)
+    torch.testing.assert_close(out.float().cpu(), want_out, rtol=2e-2, atol=1e-2)
