@@ -23,7 +23,10 @@ _DTYPE_CODE = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float
 EXPORTED_SYMBOLS = (
     "sink_abi_version", "sink_strerror", "sink_workspace_bytes", "sink_plan", "sink_append",
     "sink_evict_rerotate", "sink_decode_attention", "sink_fused_decode_step", "sink_read_status",
+    "sink_decode_attention_noalloc",
 )
+NOALLOC_SCRATCH_BYTES = 16 << 20
+ESCRATCH = -8
 
 
 class KVBuffers(ctypes.Structure):
@@ -66,6 +69,7 @@ def _declare(lib):
         "sink_fused_decode_step": (i32, [pkv, prows, prows, prows, i32, i32, i32, i32, fp, fp, i32,
                                          ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
         "sink_read_status": (i32, [vp, vp, pi32]),
+        "sink_decode_attention_noalloc": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, vp, i64, i64, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -277,3 +281,15 @@ def fused_decode_step(kbuf: torch.Tensor, vbuf: torch.Tensor, k: torch.Tensor, v
         out.stride(0), out.stride(2), buf.data_ptr(), buf.numel(), stream_handle(kbuf.device))
     _check(rc, "sink_fused_decode_step")
     return out
+
+
+def decode_attention_noalloc(q: torch.Tensor, kbuf: torch.Tensor, vbuf: torch.Tensor, rows: int, scale: float,
+                             out: torch.Tensor, mask: torch.Tensor | None = None) -> int:
+    """decode_attention without a workspace, for callers that cannot allocate device memory:
+    the library's static 16 MiB device scratch holds the split partials instead.  Returns
+    the library's code (0, or ESCRATCH when the request needs more scratch than that)."""
+    kv = kv_desc(kbuf, vbuf)
+    mptr, msb = mask_arg(mask, kbuf.shape[0], rows)
+    return lib().sink_decode_attention_noalloc(ctypes.byref(rows_desc(q)), ctypes.byref(kv), int(rows),
+                                               float(scale), mptr, msb, out.data_ptr(), out.stride(0),
+                                               out.stride(2), stream_handle(kbuf.device))

@@ -308,6 +308,7 @@ const char* sink_strerror(int32_t code) {
     case SINK_ELAYOUT: return "sinkcache_b200: cache rows must be contiguous and 16-byte aligned";
     case SINK_EWORKSPACE: return "sinkcache_b200: workspace missing or smaller than sink_workspace_bytes()";
     case SINK_EDEVICE: return "sinkcache_b200: no usable CUDA device";
+    case SINK_ESCRATCH: return "sinkcache_b200: request needs more than the 16 MiB static scratch of sink_decode_attention_noalloc; use sink_decode_attention with a workspace";
     default:
       if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));
       return "sinkcache_b200: unknown error";
@@ -516,3 +517,53 @@ int32_t sink_read_status(void* workspace, void* stream, int32_t* status) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ no-allocation variant
+
+// Scratch of sink_decode_attention_noalloc.  In host code this name is only a stand-in for
+// the symbol, not a device address: the host looks up each device's copy with
+// cudaGetSymbolAddress and passes that pointer to the kernels.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[SINK_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+// Device address of g_noalloc_scratch on device `dev` (the current device), looked up once.
+int32_t noalloc_scratch(int dev, void** ptr) {
+  static std::atomic<void*> cache[64];
+  void* p = cache[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess) return err;
+    if (p == nullptr) return SINK_EDEVICE;
+    cache[dev].store(p, std::memory_order_release);
+  }
+  *ptr = p;
+  return SINK_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t sink_decode_attention_noalloc(const sink_rows_t* q, const sink_kv_buffers_t* kv,
+                                                 int32_t rows, float scale, const uint8_t* mask,
+                                                 int64_t mask_stride_b, void* out,
+                                                 int64_t out_stride_b, int64_t out_stride_h,
+                                                 void* stream) {
+  int32_t rc = check_kv(kv);
+  if (rc) return rc;
+  if (!q || !q->data || !out) return SINK_EINVAL;
+  int dev = 0;
+  const int sms = device_sms(&dev);
+  if (sms <= 0) return SINK_EDEVICE;
+  Plan pl;
+  rc = make_plan(SINK_OP_ATTEND, kv->batch, kv->heads_kv, q->heads, kv->head_dim, kv->k_dtype,
+                 kv->v_dtype, rows, 0, 1, 0, sms, pl);
+  if (rc) return rc;
+  if (pl.total > SINK_NOALLOC_SCRATCH_BYTES) return SINK_ESCRATCH;
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch(dev, &scratch))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t err = cudaMemsetAsync(scratch, 0, sizeof(int32_t), st);  // status word
+  if (err != cudaSuccess) return err;
+  return sink_decode_attention(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
+                               out_stride_h, scratch, SINK_NOALLOC_SCRATCH_BYTES, stream);
+}

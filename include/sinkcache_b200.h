@@ -48,6 +48,7 @@ extern "C" {
 #define SINK_ELAYOUT (-5)     /* slots not contiguous, or a pointer not 16-byte aligned */
 #define SINK_EWORKSPACE (-6)  /* workspace missing or smaller than sink_workspace_bytes() */
 #define SINK_EDEVICE (-7)     /* no usable CUDA device */
+#define SINK_ESCRATCH (-8)    /* needs more than the static scratch of sink_decode_attention_noalloc */
 
 /* status bits written by kernels into the workspace status word */
 #define SINK_STATUS_WAIT_TIMEOUT 1
@@ -179,6 +180,34 @@ int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k
 
 /* Copy the workspace status word to *status (synchronises `stream`) and clear it. */
 int32_t sink_read_status(void* workspace, void* stream, int32_t* status);
+
+/* Size of the static device scratch behind sink_decode_attention_noalloc: 16 MiB. */
+#define SINK_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/*
+ * sink_decode_attention without a caller-provided workspace.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory -- a binding from a
+ * foreign runtime that has no device allocator of its own (a C or FFI host outside
+ * PyTorch), or a decode loop that must not call cudaMalloc / cudaFree because those
+ * synchronise the device and stall the stream.  Same arguments and results as
+ * sink_decode_attention minus the workspace; the split partials live instead in a
+ * file-scope 16 MiB device array (SINK_NOALLOC_SCRATCH_BYTES) that every GPU which loads
+ * the library holds until the process exits.
+ *   - The first call on a device looks up that device's copy of the array
+ *     (cudaGetSymbolAddress, with the device current); make that first call before any
+ *     stream capture.
+ *   - A request whose scratch (sink_workspace_bytes(SINK_OP_ATTEND, ...)) exceeds the array
+ *     returns SINK_ESCRATCH and launches nothing.
+ *   - All calls share the one array and each call leaves its partials there: calls that can
+ *     overlap on the GPU (different streams, different host threads) race and must be
+ *     serialised by the caller.  Each call clears the array's status word first; the
+ *     bounded-wait status is not reported through this entry point.
+ *   - Allocates nothing: no cudaMalloc, cudaFree or allocating library routine.
+ */
+int32_t sink_decode_attention_noalloc(const sink_rows_t* q, const sink_kv_buffers_t* kv,
+                                      int32_t rows, float scale, const uint8_t* mask,
+                                      int64_t mask_stride_b, void* out, int64_t out_stride_b,
+                                      int64_t out_stride_h, void* stream);
 
 #ifdef __cplusplus
 }
