@@ -315,6 +315,126 @@ def sweep(device: torch.device, flush: torch.Tensor) -> dict:
     return out
 
 
+# ----------------------------------------------------------------------------- model workloads
+
+
+def model_configs():
+    """The model-level configurations: random-init architectures (no weights available)."""
+    from transformers import LlamaConfig, Qwen3Config
+    qwen3_06b = dict(vocab_size=151936, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                     num_attention_heads=16, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
+                     max_position_embeddings=40960, tie_word_embeddings=True, rms_norm_eps=1e-6)
+    return {
+        # BASELINE config 1: Qwen3-0.6B, sink 4 + window 1020, 1 stream
+        "qwen3-0.6b-1k": dict(cfg=lambda: Qwen3Config(**qwen3_06b), n_sink=4, window=1020, streams=1,
+                              partition=False),
+        # config 3: Llama-3.2-1B (llama3 rope scaling), 1K slots, 8 streams
+        "llama3.2-1b-1k": dict(cfg=lambda: LlamaConfig(
+            vocab_size=128256, hidden_size=2048, intermediate_size=8192, num_hidden_layers=16,
+            num_attention_heads=32, num_key_value_heads=8, head_dim=64, rope_theta=5e5,
+            rope_scaling={"rope_type": "llama3", "factor": 32.0, "low_freq_factor": 1.0,
+                          "high_freq_factor": 4.0, "original_max_position_embeddings": 8192},
+            max_position_embeddings=131072, tie_word_embeddings=True, rms_norm_eps=1e-5),
+            n_sink=4, window=1020, streams=8, partition=False),
+        # config 4: Qwen3-0.6B with 32,768 slots, 32 streams split over the GPUs (16 per wave)
+        "qwen3-0.6b-32k": dict(cfg=lambda: Qwen3Config(**qwen3_06b), n_sink=4, window=32764, streams=32,
+                               partition=True, wave=16),
+        # config 5: Qwen3-8B, 4,096 slots, 16 streams per GPU
+        "qwen3-8b-4k": dict(cfg=lambda: Qwen3Config(
+            vocab_size=151936, hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
+            num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
+            max_position_embeddings=40960, tie_word_embeddings=False, rms_norm_eps=1e-6),
+            n_sink=4, window=4092, streams=16, partition=False),
+    }
+
+
+class ModelBench:
+    """One model replica and `streams` sink caches on one GPU, filled to the steady state
+    (n_sink + window kept rows + one pending) through SinkLayer.update with synthetic K/V,
+    then streamed one token per step under the CUDA-graph StreamRunner."""
+
+    def __init__(self, spec: dict, streams_: int, device: torch.device, seed: int):
+        from transformers import AutoModelForCausalLM
+
+        from attention_sinks_b200 import SinkCache, StreamRunner, register
+        name = register()
+        cfg = spec["cfg"]()
+        torch.manual_seed(seed)
+        with torch.device(device):
+            self.model = AutoModelForCausalLM.from_config(cfg, attn_implementation=name,
+                                                          dtype=torch.bfloat16).eval()
+        self.cfg, self.batch, self.device = cfg, streams_, device
+        self.cache = SinkCache.from_model(self.model, n_sink=spec["n_sink"], window=spec["window"])
+        hkv, d = cfg.num_key_value_heads, cfg.head_dim
+        rows = spec["n_sink"] + spec["window"] + 1
+        g = torch.Generator(device=device).manual_seed(seed)
+        for layer in self.cache.layers:
+            for r0 in range(0, rows, 4096):
+                n = min(4096, rows - r0)
+                k = torch.randn(streams_, hkv, n, d, device=device, generator=g).to(torch.bfloat16)
+                v = torch.randn(streams_, hkv, n, d, device=device, generator=g).to(torch.bfloat16)
+                layer.update(k, v)
+        self.runner = StreamRunner(self.model, self.cache)
+        self.ids = torch.randint(0, cfg.vocab_size, (streams_, 64), device=device, generator=g)
+        self.nll = torch.zeros(streams_, device=device)
+
+    def step(self, i: int) -> None:
+        import torch.nn.functional as F
+        j = i % (self.ids.shape[1] - 1)
+        logits = self.runner.step(self.ids[:, j:j + 1])[:, -1]
+        self.nll += F.cross_entropy(logits.float(), self.ids[:, j + 1], reduction="none")
+
+    def cache_bytes(self) -> int:
+        return sum(l._kbuf.numel() * l._kbuf.element_size() + l._vbuf.numel() * l._vbuf.element_size()
+                   for l in self.cache.layers)
+
+
+def run_model(args, workload: str) -> None:
+    from attention_sinks_b200 import streams
+    spec = model_configs()[workload]
+    rank, world, local = streams.init_from_env("nccl")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    total = spec["streams"] * (world if not spec["partition"] else 1)
+    mine = len(streams.shard(spec["streams"], rank, world)) if spec["partition"] else spec["streams"]
+    wave = spec.get("wave", mine)
+    waves = [min(wave, mine - w0) for w0 in range(0, mine, wave)]
+    elapsed, launches = 0.0, 0
+    for wi, nb in enumerate(waves):
+        bench = ModelBench(spec, nb, device, seed=1000 * rank + wi)
+        for i in range(args.warmup):  # eager steps (eviction starts), capture, replays
+            bench.step(i)
+        assert bench.cache.is_steady and bench.runner.graph is not None
+        torch.cuda.synchronize()
+        streams.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(args.steps):
+            bench.step(args.warmup + i)
+        end.record()
+        end.synchronize()
+        elapsed += start.elapsed_time(end) / 1e3
+        launches += 3 * bench.cfg.num_hidden_layers * args.steps
+        cache_gb = bench.cache_bytes() / 1e9
+        del bench
+        torch.cuda.empty_cache()
+    t_max = streams.reduce_max(elapsed)
+    tok = streams.reduce_sum([mine * args.steps])[0]
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(tok / t_max, 1), "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_max * 1e3 / args.steps, 4),
+                "higher_is_better": True, "scaling": "strong" if spec["partition"] else "weak",
+                "vs_baseline": None, "dtype": "bf16 model / fp32 K", "data": "synthetic (random-init weights, "
+                "uniform tokens, cache filled to the steady state)",
+                "config": {"workload": workload, "streams_total": total, "streams_per_gpu": mine,
+                           "waves_per_gpu": len(waves), "n_sink": spec["n_sink"], "window": spec["window"],
+                           "layers": model_configs()[workload]["cfg"]().num_hidden_layers,
+                           "cache_gb_per_wave": round(cache_gb, 2), "runner": "StreamRunner (CUDA graph)"},
+                "gpu_launches": launches}
+        print(json.dumps(line), flush=True)
+    streams.shutdown()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -325,9 +445,13 @@ def main():
     ap.add_argument("--streams", type=int, default=64, help="streams per GPU")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="op", choices=["op"] + sorted(model_configs()),
+                    help="op: the fused layer-step (default); otherwise a model-level streamed run")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.workload != "op":
+        return run_model(args, args.workload)
 
     from attention_sinks_b200 import streams
     world_env = int(os.environ.get("WORLD_SIZE", "1"))

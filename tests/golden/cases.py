@@ -106,6 +106,22 @@ def qwen3_0_6b(steps, attn="sdpa", batch=1, seed=1):
     return model, ids
 
 
+def tiny_llama3_stream_config():
+    """Llama-3.2 geometry (32 q / 8 kv heads, head_dim 64, theta 5e5, llama3 scaling), 2 layers."""
+    from transformers import LlamaConfig
+    return LlamaConfig(vocab_size=512, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                       num_attention_heads=32, num_key_value_heads=8, head_dim=64, rope_theta=5e5,
+                       rope_scaling={"rope_type": "llama3", "factor": 32.0, "low_freq_factor": 1.0,
+                                     "high_freq_factor": 4.0, "original_max_position_embeddings": 8192},
+                       max_position_embeddings=131072, tie_word_embeddings=True, rms_norm_eps=1e-5)
+
+
+def tiny_llama3_stream(dtype, attn="sdpa", n_tokens=301, batch=2):
+    model = build_model(tiny_llama3_stream_config(), dtype, attn)
+    ids = torch.randint(0, 512, (batch, n_tokens), generator=torch.Generator().manual_seed(2))
+    return model, ids
+
+
 def tiny_llama3():
     from transformers import LlamaConfig
     cfg = LlamaConfig(vocab_size=256, hidden_size=256, intermediate_size=512, num_hidden_layers=1,

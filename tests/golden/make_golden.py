@@ -157,6 +157,27 @@ def stream_case(ref, out, arrays):
     arrays["stream/kept_k_rowsum"] = np.stack([k.double().sum(-1).numpy() for k, _ in kept])
 
 
+def llama_stream_case(ref, out, arrays):
+    """Tiny Llama-3.2-shaped model (llama3 rope scaling, GQA 4, head_dim 64), batch 2,
+    streamed through the reference SinkCache (4, 60): per-token NLL of both streams."""
+    from sinkcache import SinkCache
+    model, ids = cases.tiny_llama3_stream(torch.float32)
+    cache = SinkCache.from_model(model, n_sink=4, window=60)
+    nll = []
+    import torch.nn.functional as F
+    with torch.no_grad():
+        logits = model(ids[:, :16], past_key_values=cache, use_cache=True).logits[:, -1]
+        nll.append(F.cross_entropy(logits.float(), ids[:, 16], reduction="none"))
+        for t in range(16, ids.shape[1] - 1):
+            logits = model(ids[:, t:t + 1], past_key_values=cache, use_cache=True).logits[:, -1]
+            nll.append(F.cross_entropy(logits.float(), ids[:, t + 1], reduction="none"))
+    nll = torch.stack(nll, 1)
+    out["llama_stream"] = {"mean_nll": float(nll.mean()), "tokens_evicted": cache.tokens_evicted,
+                           "ids": digest(ids)}
+    arrays["llama_stream/nll"] = nll.numpy()
+    arrays["llama_stream/last_logits"] = logits.float().numpy()
+
+
 def inv_freq_case(ref, out, arrays):
     """find_inv_freq on a Llama-3.2-1B-shaped config with llama3 rope scaling."""
     from sinkcache.cache import find_inv_freq
@@ -191,7 +212,8 @@ def main():
     arrays = dict(np.load(npz_path)) if os.path.exists(npz_path) else {}
     out["meta"] = {"torch": torch.__version__, "reference": "buttaRahul/Attention_sinks src/sinkcache",
                    "transformers": __import__("transformers").__version__}
-    for fn in (evict_cases, rerotate_cases, attention_cases, step_cases, stream_case, inv_freq_case):
+    for fn in (evict_cases, rerotate_cases, attention_cases, step_cases, stream_case, llama_stream_case,
+               inv_freq_case):
         t0 = time.time()
         fn(ref, out, arrays)
         print(f"{fn.__name__}: {time.time() - t0:.1f}s", flush=True)
