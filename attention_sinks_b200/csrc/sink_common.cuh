@@ -64,15 +64,16 @@ __host__ __device__ inline void split_rows(int row_begin, int row_end, int rows_
   e = imin(a + rows_per_split, row_end);
 }
 
-// Source rows of split j that another split of the same launch may overwrite before split j
-// reads them: they are copied to the halo workspace by a pre-pass.  [hlo, hhi) in buffer-row
-// space; empty when hlo >= hhi.  Split j's window sources are [max(a, s) + drop,
-// min(e, s + W) + drop); rows below e belong to split j itself (read before written, in
-// order); rows from e up to `written_end` (exclusive) are destinations of later splits.
+// Source rows of the split of rows [a, e) that another split of the same launch may
+// overwrite before this split reads them (none for the last split of a pair).  [hlo, hhi)
+// in buffer-row space; empty when hlo >= hhi.  The split's window sources are
+// [max(a, s) + drop, min(e, s + W) + drop); rows below e belong to the split itself (read
+// before written, in order); rows from e up to `written_end` (exclusive) are destinations of
+// later splits.
 __host__ __device__ inline void halo_range(int n_sink, int window, int drop, int written_end,
-                                           int ns, int j, int a, int e, int& hlo, int& hhi) {
+                                           bool last, int a, int e, int& hlo, int& hhi) {
   hlo = hhi = 0;
-  if (drop <= 0 || j >= ns - 1) return;
+  if (drop <= 0 || last) return;
   const int w0 = imax(a, n_sink), w1 = imin(e, n_sink + window);
   if (w0 >= w1) return;
   const int s0 = w0 + drop, s1 = w1 + drop;

@@ -50,35 +50,42 @@ bool geometry(int D, int ks, int vs, Plan& pl) {
   return true;
 }
 
-// Splits per (batch, head) pair: the smallest count that minimises waves x chunks per split,
-// so the grid fills every SM slot without a long tail.
+// Split plan: every (batch, head) pair's rows cut into `ns` items of `tps` chunks, one CTA
+// each.  Two regimes, from measurements over the op-bench grid on B200:
+//   - a step whose pairs fit in one wave of CTAs with items of at most kMaxItemChunks
+//     chunks takes exactly one wave: as many splits per pair as there are free SM slots
+//     per pair (few pairs with long rows: every SM streams one long item);
+//   - otherwise items of kMinItemChunks..kMaxItemChunks chunks, aiming at kTargetWaves
+//     waves, so the block scheduler evens out SMs that stream at different rates.
+constexpr long kMinItemChunks = 4;
+constexpr long kMaxItemChunks = 32;
+constexpr long kTargetWaves = 16;
+
 void choose_splits(int pairs, int rows, int T, int slots, Plan& pl) {
-  const int tiles = (rows + T - 1) / T;
-  long best = LONG_MAX;
-  int best_ns = 1, best_tps = tiles;
-  const int max_ns = tiles < kMaxSplits ? tiles : kMaxSplits;
-  for (int n = 1; n <= max_ns; ++n) {
-    const int tps = (tiles + n - 1) / n;
-    const int ne = (tiles + tps - 1) / tps;
-    if (ne != n) continue;
-    const long items = long(pairs) * ne;
-    const long waves = (items + slots - 1) / slots;
-    const long cost = waves * tps;
-    if (cost < best) {
-      best = cost;
-      best_ns = ne;
-      best_tps = tps;
-    }
+  const long tiles = (rows + T - 1) / T;
+  const long total = long(pairs) * tiles;
+  long ns;
+  if (long(pairs) * ((tiles + kMaxItemChunks - 1) / kMaxItemChunks) <= slots) {
+    ns = slots / pairs;
+  } else {
+    long tps = (total + kTargetWaves * slots - 1) / (kTargetWaves * slots);
+    tps = tps < kMinItemChunks ? kMinItemChunks : (tps > kMaxItemChunks ? kMaxItemChunks : tps);
+    ns = (tiles + tps - 1) / tps;
   }
-  pl.ns = best_ns;
-  pl.rows_per_split = best_tps * T;
+  if (ns > tiles) ns = tiles;
+  if (ns > kMaxSplits) ns = kMaxSplits;
+  if (ns < 1) ns = 1;
+  const long tps = (tiles + ns - 1) / ns;  // even the items out
+  pl.ns = int((tiles + tps - 1) / tps);
+  pl.rows_per_split = int(tps) * T;
 }
 
 int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, int32_t D,
                   int32_t kdt, int32_t vdt, int32_t rows, int32_t n_sink, int32_t window,
                   int32_t drop, int32_t num_sms, Plan& pl) {
   pl = Plan();
-  if (batch < 1 || heads_kv < 1 || num_sms < 1) return SINK_EINVAL;
+  if (batch < 1 || heads_kv < 1 || num_sms < 1 || num_sms > 4096) return SINK_EINVAL;
+  if (long(batch) * heads_kv > (1L << 24)) return SINK_EINVAL;  // pair indices stay in int
   if (!supported_types(kdt, vdt)) return SINK_EDTYPE;
   const int ks = elem_size(kdt), vs = elem_size(vdt);
   if (!geometry(D, ks, vs, pl)) return SINK_EHEADDIM;

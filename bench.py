@@ -194,6 +194,15 @@ class OpBench:
         return self.k.numel() * 4 + self.v.numel() * 2
 
 
+def flush_l2(buf: torch.Tensor, i: int) -> None:
+    """Evict the state from L2 between timed steps: write one half of `buf` (2x L2), then
+    read the other half, so L2 is left holding clean lines and the timed step does not
+    pay for writing back the flush's dirty lines."""
+    half = buf.numel() // 2
+    buf[:half].fill_(i & 0xFF)
+    buf[half:].sum(dtype=torch.int64)
+
+
 def time_device(bench: OpBench, steps: int, warmup: int, flush: torch.Tensor | None = None) -> float:
     """Mean ms per step with CUDA events on the launching stream.  When `flush` is given
     (state smaller than L2), L2 is overwritten between steps and each step timed alone."""
@@ -210,7 +219,7 @@ def time_device(bench: OpBench, steps: int, warmup: int, flush: torch.Tensor | N
         return start.elapsed_time(end) / steps
     total = 0.0
     for i in range(steps):
-        flush.fill_(i & 0xFF)
+        flush_l2(flush, i)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         bench.step(i)
@@ -298,15 +307,52 @@ def cpu_baseline(slots: int, seconds: float = 15.0) -> dict:
                       f"SinkLayer.update (PyTorch path) + SDPA, torch threads={threads}"}
 
 
+def time_graph(bench: OpBench, steps: int, flush: torch.Tensor | None) -> float:
+    """Mean ms per step of one captured step replayed from a CUDA graph (how StreamRunner
+    runs it: no host launch cost inside the step).  With `flush`, L2 is overwritten between
+    replays and each replay is timed alone."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for i in range(3):
+            bench.step(0)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        bench.step(0)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    if flush is None:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            graph.replay()
+        end.record()
+        end.synchronize()
+        return start.elapsed_time(end) / steps
+    total = 0.0
+    for i in range(steps):
+        flush_l2(flush, i)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        graph.replay()
+        end.record()
+        end.synchronize()
+        total += start.elapsed_time(end)
+    return total / steps
+
+
 def sweep(device: torch.device, flush: torch.Tensor) -> dict:
-    """µs per layer-step and GB/s over the op-bench grid (slots x streams), 1 GPU."""
+    """µs per layer-step and GB/s over the op-bench grid (slots x streams), 1 GPU, from
+    CUDA-graph replays (L2 flushed between replays when the state is smaller than 2x L2)."""
     out = {}
     for slots in (256, 1024, 4096, 32768):
         for batch in (1, 8, 64):
             b = OpBench(batch, slots, device, seed=slots + batch)
             small = b.state_bytes() < 2 * L2_BYTES
             steps = 50 if small else max(10, min(200, int(2e9 / (alg_bytes(slots) * batch))))
-            ms = time_device(b, steps, 3, flush if small else None)
+            ms = time_graph(b, steps, flush if small else None)
             out[f"S{slots}_B{batch}"] = {"us_per_layer": round(ms * 1e3, 2),
                                         "GB_s": round(alg_bytes(slots) * batch / (ms * 1e-3) / 1e9, 1),
                                         "l2_flushed": small}
@@ -487,7 +533,11 @@ def main():
     build.build()  # no-op when the shipped library is current
 
     bench = OpBench(args.streams, args.slots, device, seed=1000 + rank)
-    assert bench.state_bytes() > 2 * L2_BYTES
+    small = bench.state_bytes() < 2 * L2_BYTES
+    if small:
+        config["l2"] = ("state smaller than 2x L2: between steps 256 MB written then 256 MB read (L2 left "
+                        "clean), each step timed alone")
+    l2_flush = torch.empty(512 * 2 ** 20, dtype=torch.uint8, device=device) if small else None
     for i in range(args.warmup):
         bench.step(i)
     torch.cuda.synchronize()
@@ -495,7 +545,7 @@ def main():
     torch.cuda.synchronize()
     clocks = ClockSampler(device)
     clocks.start()
-    ms = time_device(bench, args.steps, 0)
+    ms = time_device(bench, args.steps, 0, l2_flush)
     clk = clocks.stop()
     torch.cuda.synchronize()
     streams.barrier()
@@ -534,7 +584,7 @@ def main():
     extra = {}
     if world == 1 and rank == 0:
         if not args.no_sweep:
-            flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=device)
+            flush = torch.empty(512 * 2 ** 20, dtype=torch.uint8, device=device)
             del bench
             torch.cuda.empty_cache()
             extra["sweep"] = sweep(device, flush)

@@ -192,7 +192,8 @@ int32_t sink_read_status(void* workspace, void* stream, int32_t* status);
  * synchronise the device and stall the stream.  Same arguments and results as
  * sink_decode_attention minus the workspace; the split partials live instead in a
  * file-scope 16 MiB device array (SINK_NOALLOC_SCRATCH_BYTES) that every GPU which loads
- * the library holds until the process exits.
+ * the library holds until the process exits (on a B200 it holds, e.g., 16 streams of a
+ * 32K-slot Qwen3 layer).
  *   - The first call on a device looks up that device's copy of the array
  *     (cudaGetSymbolAddress, with the device current); make that first call before any
  *     stream capture.

@@ -44,15 +44,17 @@ def test_noalloc_matches_workspace_entry_point(built_lib):
 
 
 def test_noalloc_refuses_requests_beyond_its_scratch(built_lib):
-    batch, rows = 16, 32769
-    need = _lib.workspace_bytes(_lib.OP_ATTEND, batch, 8, 16, 128, torch.float32, torch.bfloat16, rows, 0, 1, 0,
+    # 16 streams x 8 kv heads with groups of 8 query heads at head_dim 256 need more split
+    # partials than the static array holds
+    batch, hkv, hq, d, rows = 16, 8, 64, 256, 4097
+    need = _lib.workspace_bytes(_lib.OP_ATTEND, batch, hkv, hq, d, torch.float32, torch.bfloat16, rows, 0, 1, 0,
                                 _lib.sm_count(torch.device(DEV)))
     assert need > _lib.NOALLOC_SCRATCH_BYTES
-    k = torch.empty(batch, 8, rows, 128, dtype=torch.float32, device=DEV)
-    v = torch.empty(batch, 8, rows, 128, dtype=torch.bfloat16, device=DEV)
-    q = torch.zeros(batch, 16, 1, 128, dtype=torch.bfloat16, device=DEV)
-    out = torch.full((batch, 1, 16, 128), 7.0, dtype=torch.bfloat16, device=DEV)
-    rc = _lib.decode_attention_noalloc(q, k, v, rows, 0.088, out)
+    k = torch.zeros(batch, hkv, rows, d, dtype=torch.float32, device=DEV)
+    v = torch.zeros(batch, hkv, rows, d, dtype=torch.bfloat16, device=DEV)
+    q = torch.zeros(batch, hq, 1, d, dtype=torch.bfloat16, device=DEV)
+    out = torch.full((batch, 1, hq, d), 7.0, dtype=torch.bfloat16, device=DEV)
+    rc = _lib.decode_attention_noalloc(q, k, v, rows, 0.0625, out)
     assert rc == _lib.ESCRATCH
     assert "16 MiB" in _lib.strerror(rc)
     torch.cuda.synchronize()
