@@ -23,7 +23,7 @@ _DTYPE_CODE = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float
 EXPORTED_SYMBOLS = (
     "sink_abi_version", "sink_strerror", "sink_workspace_bytes", "sink_plan", "sink_append",
     "sink_evict_rerotate", "sink_decode_attention", "sink_fused_decode_step", "sink_read_status",
-    "sink_decode_attention_noalloc",
+    "sink_decode_attention_noalloc", "sink_v2_place", "sink_v2_decode_step",
 )
 NOALLOC_SCRATCH_BYTES = 16 << 20
 ESCRATCH = -8
@@ -70,6 +70,9 @@ def _declare(lib):
                                          ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
         "sink_read_status": (i32, [vp, vp, pi32]),
         "sink_decode_attention_noalloc": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, vp, i64, i64, vp]),
+        "sink_v2_place": (i32, [pkv, prows, prows, prows, vp, i32, prows, vp, i64, i32, i32, vp, i32, vp]),
+        "sink_v2_decode_step": (i32, [pkv, prows, prows, prows, vp, i32, vp, i32, i32, vp, i32, prows,
+                                      ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -230,18 +233,19 @@ def evict_rerotate(kbuf: torch.Tensor, vbuf: torch.Tensor, n_sink: int, window: 
     _check(rc, "sink_evict_rerotate")
 
 
-def mask_arg(mask: torch.Tensor | None, batch: int, rows: int) -> tuple[int | None, int]:
-    """(pointer, batch stride in bytes) of a boolean [B or 1, 1, 1, rows] attention mask for
-    a one-token query (True = attend), as the kernels take it."""
+def mask_arg(mask: torch.Tensor | None, batch: int, rows: int) -> tuple[int | None, int, torch.Tensor | None]:
+    """(pointer, batch stride in bytes, tensor to keep alive until the launch) of a boolean
+    [B or 1, 1, 1, rows] attention mask for a one-token query (True = attend), as the
+    kernels take it."""
     if mask is None:
-        return None, 0
+        return None, 0, None
     if (mask.dtype != torch.bool or mask.dim() != 4 or mask.shape[1] != 1 or mask.shape[2] != 1
             or mask.shape[3] != rows or mask.shape[0] not in (1, batch)):
         raise ValueError(f"kernel masks are boolean [B, 1, 1, {rows}], got {mask.dtype} {tuple(mask.shape)}")
     _require_cuda(mask)
     if mask.stride(-1) != 1:
         mask = mask.contiguous()
-    return mask.data_ptr(), (mask.stride(0) if mask.shape[0] > 1 else 0)
+    return mask.data_ptr(), (mask.stride(0) if mask.shape[0] > 1 else 0), mask
 
 
 def decode_attention(q: torch.Tensor, kbuf: torch.Tensor, vbuf: torch.Tensor, rows: int, scale: float,
@@ -253,7 +257,7 @@ def decode_attention(q: torch.Tensor, kbuf: torch.Tensor, vbuf: torch.Tensor, ro
     need = workspace_bytes(OP_ATTEND, b, h, q.shape[1], d, kbuf.dtype, vbuf.dtype, rows, 0, 1, 0,
                            sm_count(kbuf.device))
     buf = ws.get(need, kbuf.device)
-    mptr, msb = mask_arg(mask, b, rows)
+    mptr, msb, _keep = mask_arg(mask, b, rows)
     rc = lib().sink_decode_attention(ctypes.byref(rows_desc(q)), ctypes.byref(kv), int(rows), float(scale),
                                      mptr, msb, out.data_ptr(), out.stride(0), out.stride(2), buf.data_ptr(),
                                      buf.numel(), stream_handle(kbuf.device))
@@ -273,7 +277,7 @@ def fused_decode_step(kbuf: torch.Tensor, vbuf: torch.Tensor, k: torch.Tensor, v
                            n_sink, window, drop, sm_count(kbuf.device))
     buf = ws.get(need, kbuf.device)
     rotate = cos is not None
-    mptr, msb = mask_arg(mask, b, append_row + 1)
+    mptr, msb, _keep = mask_arg(mask, b, append_row + 1)
     rc = lib().sink_fused_decode_step(
         ctypes.byref(kv), ctypes.byref(rows_desc(k)), ctypes.byref(rows_desc(v)), ctypes.byref(rows_desc(q)),
         n_sink, window, drop, append_row, cos.data_ptr() if rotate else None,
@@ -289,7 +293,74 @@ def decode_attention_noalloc(q: torch.Tensor, kbuf: torch.Tensor, vbuf: torch.Te
     the library's static 16 MiB device scratch holds the split partials instead.  Returns
     the library's code (0, or ESCRATCH when the request needs more scratch than that)."""
     kv = kv_desc(kbuf, vbuf)
-    mptr, msb = mask_arg(mask, kbuf.shape[0], rows)
+    mptr, msb, _keep = mask_arg(mask, kbuf.shape[0], rows)
     return lib().sink_decode_attention_noalloc(ctypes.byref(rows_desc(q)), ctypes.byref(kv), int(rows),
                                                float(scale), mptr, msb, out.data_ptr(), out.stride(0),
                                                out.stride(2), stream_handle(kbuf.device))
+
+
+# ------------------------------------------------------------------ ring-buffer (v2) layer
+
+
+def _region_args(reg_k: torch.Tensor | None, reg_pos: torch.Tensor | None, R: int,
+                 inv_freq: torch.Tensor | None):
+    if R == 0:
+        return None, None, None, 0
+    _require_cuda(reg_k, reg_pos, inv_freq)
+    if reg_pos.dtype != torch.int64 or inv_freq.dtype != torch.float64:
+        raise TypeError("region positions are int64 and inv_freq float64 on the device")
+    if not reg_pos.is_contiguous() or not inv_freq.is_contiguous():
+        raise ValueError("region positions and inv_freq must be contiguous")
+    return ctypes.byref(rows_desc(reg_k)), reg_pos.data_ptr(), inv_freq.data_ptr(), inv_freq.numel()
+
+
+def _position_arg(position: torch.Tensor | None):
+    if position is None:
+        return None
+    _require_cuda(position)
+    if position.dtype != torch.int64 or position.numel() != 2 or not position.is_contiguous():
+        raise ValueError("position is a contiguous device int64 tensor {t, 0}")
+    return position.data_ptr()
+
+
+def v2_place(kbuf: torch.Tensor, vbuf: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor | None,
+             reg_k: torch.Tensor | None, reg_pos: torch.Tensor | None, R: int,
+             region_out: torch.Tensor | None, position: torch.Tensor | None, t: int, n_sink: int,
+             window: int, inv_freq: torch.Tensor | None) -> None:
+    """Ring-buffer layer place step (cache_v2.py:171-176, :101-116): (k, v) into ring slot
+    (t - n_sink) mod (window + 1); region keys reg_k[:, :, :R] (original rotations, positions
+    reg_pos[:R]) rotated to sit just before the window, into `region_out` rows [0, R) or,
+    when it is None, the cache rows after the ring.  t comes from the device tensor
+    `position` = {t, 0} (advanced by one) or, when that is None, from the host int `t`."""
+    kv = kv_desc(kbuf, vbuf)
+    rk, rp, inv, rot_half = _region_args(reg_k, reg_pos, R, inv_freq)
+    kd = ctypes.byref(rows_desc(k)) if k is not None else None
+    vd = ctypes.byref(rows_desc(v)) if v is not None else None
+    od = ctypes.byref(rows_desc(region_out)) if region_out is not None else None
+    rc = lib().sink_v2_place(ctypes.byref(kv), kd, vd, rk, rp, int(R), od, _position_arg(position),
+                             int(t), int(n_sink), int(window), inv, int(rot_half), stream_handle(kbuf.device))
+    _check(rc, "sink_v2_place")
+
+
+def v2_decode_step(kbuf: torch.Tensor, vbuf: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                   reg_k: torch.Tensor | None, reg_pos: torch.Tensor | None, R: int,
+                   position: torch.Tensor, n_sink: int, window: int, inv_freq: torch.Tensor | None,
+                   q: torch.Tensor, scale: float, out: torch.Tensor, ws: Workspace,
+                   mask: torch.Tensor | None = None) -> torch.Tensor:
+    """Ring-buffer layer decode step (cache_v2.py:167-181) fused with its attention over the
+    window + 1 + R rows: place as v2_place, then split-K decode attention."""
+    kv = kv_desc(kbuf, vbuf)
+    b, h, _, d = kbuf.shape
+    rows = window + 1 + R
+    need = workspace_bytes(OP_ATTEND, b, h, q.shape[1], d, kbuf.dtype, vbuf.dtype, rows, 0, 1, 0,
+                           sm_count(kbuf.device))
+    buf = ws.get(need, kbuf.device)
+    rk, rp, inv, rot_half = _region_args(reg_k, reg_pos, R, inv_freq)
+    mptr, msb, _keep = mask_arg(mask, b, rows)
+    rc = lib().sink_v2_decode_step(
+        ctypes.byref(kv), ctypes.byref(rows_desc(k)), ctypes.byref(rows_desc(v)), rk, rp, int(R),
+        _position_arg(position), int(n_sink), int(window), inv, int(rot_half), ctypes.byref(rows_desc(q)),
+        float(scale), mptr, msb, out.data_ptr(), out.stride(0), out.stride(2), buf.data_ptr(), buf.numel(),
+        stream_handle(kbuf.device))
+    _check(rc, "sink_v2_decode_step")
+    return out

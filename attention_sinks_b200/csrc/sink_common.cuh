@@ -161,6 +161,17 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start before its predecessor ends; grid_dependency_wait() blocks until the
+// predecessor grid has completed and its memory is visible.  allow_dependents() lets the
+// next kernel of the stream start launching.  Both are no-ops without the launch attribute.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void allow_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------------ element conversions
 
 template <typename T>

@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
   const uint32_t bar0 = smem_addr(smem);
   unsigned char* stages = smem + kBarrierBytes;
 
+  grid_dependency_wait();  // halo copies (or the producers of q, k, v) complete
   const int tid = threadIdx.x;
   const int j = blockIdx.x, p = blockIdx.y;
   const int b = p / A.heads_kv, h = p - b * A.heads_kv;
@@ -186,6 +187,7 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
   }
   if (tid == 0) bulk_wait<0>();
   __syncthreads();
+  allow_dependents();
   if (failed) {
     if (tid == 0) atomicOr(A.status, 1);
     return;
@@ -221,26 +223,37 @@ struct HaloBytes {
   int krow, vrow;                  // bytes per row (multiples of 16)
 };
 
+// Boundaries (splits) whose halo one CTA of sink_halo_kernel copies.
+constexpr int kHaloSplitsPerCta = 8;
+
 // Copies the halo rows of every split but the last into the workspace (pre-pass of an
-// in-place shift that spans several splits).
+// in-place shift that spans several splits).  Grid: (ceil((ns - 1) / kHaloSplitsPerCta),
+// batch * heads_kv).
 __global__ void __launch_bounds__(kThreads) sink_halo_kernel(const __grid_constant__ StreamArgs A,
                                                              const HaloBytes H) {
-  const int j = blockIdx.x, p = blockIdx.y;
+  allow_dependents();  // the stream kernel may launch; it waits for this grid to complete
+  const int p = blockIdx.y;
   const int b = p / A.heads_kv, h = p - b * A.heads_kv;
-  int a, e;
-  split_rows(A.row_begin, A.row_end, A.rows_per_split, j, a, e);
-  int hlo, hhi;
-  halo_range(A.n_sink, A.window, A.drop, A.written_end, j >= A.ns - 1, a, e, hlo, hhi);
-  if (hlo >= hhi) return;
-  const size_t halo_row0 = (size_t(p) * A.ns + j) * A.halo_rows;
   const int kv4 = H.krow / (int)sizeof(uint4), vv4 = H.vrow / (int)sizeof(uint4);
-  const uint4* ks = reinterpret_cast<const uint4*>(A.kbuf + b * H.k_sb + h * H.k_sh) + size_t(hlo) * kv4;
-  const uint4* vs = reinterpret_cast<const uint4*>(A.vbuf + b * H.v_sb + h * H.v_sh) + size_t(hlo) * vv4;
-  uint4* kd = reinterpret_cast<uint4*>(A.halo_k) + halo_row0 * kv4;
-  uint4* vd = reinterpret_cast<uint4*>(A.halo_v) + halo_row0 * vv4;
-  const int nk = (hhi - hlo) * kv4, nv = (hhi - hlo) * vv4;
-  for (int i = threadIdx.x; i < nk; i += kThreads) kd[i] = ks[i];
-  for (int i = threadIdx.x; i < nv; i += kThreads) vd[i] = vs[i];
+  const uint4* kbase = reinterpret_cast<const uint4*>(A.kbuf + b * H.k_sb + h * H.k_sh);
+  const uint4* vbase = reinterpret_cast<const uint4*>(A.vbuf + b * H.v_sb + h * H.v_sh);
+  const int j0 = blockIdx.x * kHaloSplitsPerCta;
+  const int j1 = imin(j0 + kHaloSplitsPerCta, A.ns - 1);
+  for (int j = j0; j < j1; ++j) {
+    int a, e;
+    split_rows(A.row_begin, A.row_end, A.rows_per_split, j, a, e);
+    int hlo, hhi;
+    halo_range(A.n_sink, A.window, A.drop, A.written_end, false, a, e, hlo, hhi);
+    if (hlo >= hhi) continue;
+    const size_t halo_row0 = (size_t(p) * A.ns + j) * A.halo_rows;
+    const uint4* ks = kbase + size_t(hlo) * kv4;
+    const uint4* vs = vbase + size_t(hlo) * vv4;
+    uint4* kd = reinterpret_cast<uint4*>(A.halo_k) + halo_row0 * kv4;
+    uint4* vd = reinterpret_cast<uint4*>(A.halo_v) + halo_row0 * vv4;
+    const int nk = (hhi - hlo) * kv4, nv = (hhi - hlo) * vv4;
+    for (int i = threadIdx.x; i < nk; i += kThreads) kd[i] = ks[i];
+    for (int i = threadIdx.x; i < nv; i += kThreads) vd[i] = vs[i];
+  }
 }
 
 // Log-sum-exp merge of the ns split partials of every (batch, kv-head) pair.
@@ -252,6 +265,7 @@ __global__ void __launch_bounds__(kThreads) sink_combine_kernel(const float* __r
                                                                 int64_t o_sh, int heads_kv, int G,
                                                                 int ns) {
   __shared__ float wts[kMaxSplits * kMaxGroup];
+  grid_dependency_wait();  // the partials of the stream kernel are complete
   const int p = blockIdx.x;
   const int b = p / heads_kv, h = p - b * heads_kv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -1,0 +1,102 @@
+// Ring-buffer ("v2") cache step: the new token is written over one ring slot and the few
+// region keys (sinks, pinned tokens) are rotated from their stored originals to sit just
+// before the window (src/sinkcache/cache_v2.py:101-116 _rotate_region, :167-181
+// _decode_step).  Window keys are never touched; attention over ring + region is the
+// stream kernel in attend-only mode.
+#pragma once
+
+#include "sink_common.cuh"
+
+namespace sinkb200 {
+
+struct V2PlaceArgs {
+  char* kbuf;                        // ring + region slots, rows contiguous
+  char* vbuf;
+  int64_t k_sb, k_sh, v_sb, v_sh;    // element strides
+  const char* knew;                  // [B, Hkv, 1, D] new token, or null (no ring write)
+  const char* vnew;
+  int64_t kn_sb, kn_sh, vn_sb, vn_sh;
+  const char* reg_k;                 // [B, Hkv, >= R, D] region keys at their original rotation
+  int64_t rk_sb, rk_sh, rk_st;
+  char* rout;                        // [B, Hkv, >= R, D] rotated region keys
+  int64_t ro_sb, ro_sh, ro_st;
+  const int64_t* reg_pos;            // [>= R] original positions of the region tokens
+  int64_t* position;                 // {t, arrivals} on the device, or null: t_host
+  int64_t t_host;
+  const double* inv_freq;            // [rot_half]
+  int n_sink, window, ring, R, rot_half, heads_kv, pairs;
+};
+
+// One CTA per (batch, kv-head) pair (grid-strided).  t is the absolute position of the new
+// token; ws = max(min(t, n_sink), t - window) the first window position; region row j is
+// rotated by (ws - R + j) - reg_pos[j].  The angle is formed in fp64 (positions grow without
+// bound), cos/sin rounded once to fp32, and each output element is
+// fp32(fp32(x * cos) + fp32(rotate_half(x) * sin)) rounded once to the storage type: the
+// reference's three separately rounded tensor ops.  With `position`, the last CTA to finish
+// stores t + 1 (every CTA has read t before it counts itself in).
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads) sink_v2_place_kernel(V2PlaceArgs a) {
+  grid_dependency_wait();
+  allow_dependents();
+  __shared__ long long t_s;
+  if (threadIdx.x == 0) t_s = a.position ? a.position[0] : a.t_host;
+  __syncthreads();
+  const long long t = t_s;
+  long long ws = t < a.n_sink ? t : a.n_sink;
+  if (t - a.window > ws) ws = t - a.window;
+  using E = Elem<T>;
+  constexpr int kVec = 16 / sizeof(T);   // elements per 16-byte vector
+  constexpr int kRowVecs = D / kVec;
+  for (int p = blockIdx.x; p < a.pairs; p += gridDim.x) {
+    const int b = p / a.heads_kv, h = p - b * a.heads_kv;
+    if (a.knew) {
+      long long slot = (t - a.n_sink) % a.ring;
+      if (slot < 0) slot += a.ring;
+      for (int i = threadIdx.x; i < 2 * kRowVecs; i += kThreads) {
+        const bool is_v = i >= kRowVecs;
+        const int c = is_v ? i - kRowVecs : i;
+        const T* src = reinterpret_cast<const T*>(is_v ? a.vnew : a.knew) +
+                       (is_v ? b * a.vn_sb + h * a.vn_sh : b * a.kn_sb + h * a.kn_sh);
+        T* dst = reinterpret_cast<T*>(is_v ? a.vbuf : a.kbuf) +
+                 (is_v ? b * a.v_sb + h * a.v_sh : b * a.k_sb + h * a.k_sh) + slot * D;
+        reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(src)[c];
+      }
+    }
+    const T* rk = reinterpret_cast<const T*>(a.reg_k) + b * a.rk_sb + h * a.rk_sh;
+    T* ro = reinterpret_cast<T*>(a.rout) + b * a.ro_sb + h * a.ro_sh;
+    const int rh = a.rot_half, pass = D - 2 * rh;
+    const int per_row = rh + pass;
+    for (int i = threadIdx.x; i < a.R * per_row; i += kThreads) {
+      const int j = i / per_row, c = i - j * per_row;
+      const T* x = rk + j * a.rk_st;
+      T* y = ro + j * a.ro_st;
+      if (c < rh) {
+        const long long delta = ws - a.R + j - a.reg_pos[j];
+        const double ang = __dmul_rn(static_cast<double>(delta), a.inv_freq[c]);
+        const float cs = __double2float_rn(cos(ang));
+        const float sn = __double2float_rn(sin(ang));
+        const float x1 = E::to_f(x[c]), x2 = E::to_f(x[c + rh]);
+        y[c] = E::from_f(__fadd_rn(__fmul_rn(x1, cs), __fmul_rn(-x2, sn)));
+        y[c + rh] = E::from_f(__fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn)));
+      } else {
+        const int d = 2 * rh + (c - rh);
+        y[d] = x[d];
+      }
+    }
+  }
+  if (a.position) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const unsigned long long prev =
+          atomicAdd(reinterpret_cast<unsigned long long*>(a.position + 1), 1ull);
+      if (prev == gridDim.x - 1) {
+        a.position[0] = t + 1;
+        a.position[1] = 0;
+        __threadfence();
+      }
+    }
+  }
+}
+
+}  // namespace sinkb200

@@ -6,6 +6,7 @@
 
 #include "../../include/sinkcache_b200.h"
 #include "sink_kernels.cuh"
+#include "sink_v2.cuh"
 
 using namespace sinkb200;
 
@@ -167,6 +168,26 @@ int32_t check_rows(const sink_rows_t* r, int32_t dtype, int32_t batch, int32_t h
   return SINK_OK;
 }
 
+// Launch with programmatic stream serialization: the kernel may begin launching while its
+// predecessor in the stream finishes (every kernel here waits on the grid dependency before
+// touching memory), which hides the launch gap between the halo, stream and combine kernels.
+template <typename... Params, typename... Args>
+int32_t launch_dependent(void (*kern)(Params...), dim3 grid, int smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = size_t(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (err != cudaSuccess) return err;
+  return cudaGetLastError();
+}
+
 template <typename KT, typename VT, int D, int GMAX, bool ATTEND>
 int32_t launch_stream(const StreamArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev) {
   using Gm = StreamGeom<KT, VT, D>;
@@ -179,8 +200,7 @@ int32_t launch_stream(const StreamArgs& A, const Plan& pl, int pairs, cudaStream
     if (err != cudaSuccess) return err;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
-  kern<<<dim3(pl.ns, pairs), kThreads, Gm::SMEM, st>>>(A);
-  return cudaGetLastError();
+  return launch_dependent(kern, dim3(pl.ns, pairs), Gm::SMEM, st, A);
 }
 
 template <bool ATTEND, typename KT, typename VT, int D>
@@ -225,17 +245,19 @@ template <typename VT>
 int32_t launch_combine_t(int D, const StreamArgs& A, int pairs, cudaStream_t st) {
   switch (D) {
     case 64:
-      sink_combine_kernel<VT, 64><<<pairs, kThreads, 0, st>>>(A.o_part, A.m_part, A.l_part, A.out, A.o_sb, A.o_sh, A.heads_kv, A.group, A.ns);
-      break;
+      return launch_dependent(sink_combine_kernel<VT, 64>, dim3(pairs), 0, st, (const float*)A.o_part,
+                              (const float*)A.m_part, (const float*)A.l_part, A.out, A.o_sb, A.o_sh,
+                              A.heads_kv, A.group, A.ns);
     case 128:
-      sink_combine_kernel<VT, 128><<<pairs, kThreads, 0, st>>>(A.o_part, A.m_part, A.l_part, A.out, A.o_sb, A.o_sh, A.heads_kv, A.group, A.ns);
-      break;
+      return launch_dependent(sink_combine_kernel<VT, 128>, dim3(pairs), 0, st, (const float*)A.o_part,
+                              (const float*)A.m_part, (const float*)A.l_part, A.out, A.o_sb, A.o_sh,
+                              A.heads_kv, A.group, A.ns);
     case 256:
-      sink_combine_kernel<VT, 256><<<pairs, kThreads, 0, st>>>(A.o_part, A.m_part, A.l_part, A.out, A.o_sb, A.o_sh, A.heads_kv, A.group, A.ns);
-      break;
+      return launch_dependent(sink_combine_kernel<VT, 256>, dim3(pairs), 0, st, (const float*)A.o_part,
+                              (const float*)A.m_part, (const float*)A.l_part, A.out, A.o_sb, A.o_sh,
+                              A.heads_kv, A.group, A.ns);
     default: return SINK_EHEADDIM;
   }
-  return cudaGetLastError();
 }
 
 int32_t launch_combine(int vdt, int D, const StreamArgs& A, int pairs, cudaStream_t st) {
@@ -256,7 +278,8 @@ int32_t launch_halo(const sink_kv_buffers_t* kv, const StreamArgs& A, const Plan
   H.v_sh = kv->v_stride_h * vs;
   H.krow = kv->head_dim * ks;
   H.vrow = kv->head_dim * vs;
-  sink_halo_kernel<<<dim3(pl.ns - 1, pairs), kThreads, 0, st>>>(A, H);
+  const int cx = (pl.ns - 1 + kHaloSplitsPerCta - 1) / kHaloSplitsPerCta;
+  sink_halo_kernel<<<dim3(cx, pairs), kThreads, 0, st>>>(A, H);
   return cudaGetLastError();
 }
 
@@ -284,6 +307,50 @@ void fill_common(StreamArgs& A, const sink_kv_buffers_t* kv, const Plan& pl, cha
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Checks shared by the attention entry points, and the plan they launch with.
+int32_t plan_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows, void* out,
+                       void* workspace, size_t workspace_bytes, Plan& pl, int* dev) {
+  if (!q || !q->data || !out) return SINK_EINVAL;
+  if (q->dtype != kv->v_dtype) return SINK_EDTYPE;
+  if (q->n != 1 || rows < 1 || rows > kv->slots) return SINK_EINVAL;
+  const int sms = device_sms(dev);
+  if (sms <= 0) return SINK_EDEVICE;
+  const int32_t rc = make_plan(SINK_OP_ATTEND, kv->batch, kv->heads_kv, q->heads, kv->head_dim,
+                               kv->k_dtype, kv->v_dtype, rows, 0, 1, 0, sms, pl);
+  if (rc) return rc;
+  if (!workspace || workspace_bytes < pl.total || !aligned16(workspace)) return SINK_EWORKSPACE;
+  return SINK_OK;
+}
+
+// Split-K decode attention over rows [0, rows): stream kernel in attend-only mode + combine.
+int32_t launch_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows,
+                         float scale, const uint8_t* mask, int64_t mask_stride_b, void* out,
+                         int64_t out_stride_b, int64_t out_stride_h, void* workspace,
+                         const Plan& pl, int dev, cudaStream_t st) {
+  int32_t rc;
+  StreamArgs A;
+  fill_common(A, kv, pl, static_cast<char*>(workspace));
+  A.group = q->heads / kv->heads_kv;
+  A.q = static_cast<const char*>(q->data);
+  A.q_sb = q->stride_b;
+  A.q_sh = q->stride_h;
+  A.out = static_cast<char*>(out);
+  A.o_sb = out_stride_b;
+  A.o_sh = out_stride_h;
+  A.window = 1;
+  A.row_begin = 0;
+  A.row_end = rows;
+  A.written_end = 0;
+  A.scale_log2 = scale * kLog2e;
+  A.mask = mask;
+  A.mask_sb = mask_stride_b;
+  const int pairs = kv->batch * kv->heads_kv;
+  if ((rc = dispatch_stream<true>(kv->k_dtype, kv->v_dtype, kv->head_dim, A.group, A, pl, pairs, st, dev)))
+    return rc;
+  if (pl.ns > 1) return launch_combine(kv->v_dtype, kv->head_dim, A, pairs, st);
+  return SINK_OK;
+}
+
 template <typename KT, typename VT>
 int32_t launch_append_t(const sink_kv_buffers_t* kv, const sink_rows_t* kn, const sink_rows_t* vn,
                         int32_t row, cudaStream_t st) {
@@ -297,6 +364,104 @@ int32_t launch_append_t(const sink_kv_buffers_t* kv, const sink_rows_t* kn, cons
       static_cast<const VT*>(vn->data), kn->stride_b, kn->stride_h, kn->stride_t, vn->stride_b,
       vn->stride_h, vn->stride_t, kv->heads_kv, kn->n, kv->head_dim, row, total);
   return cudaGetLastError();
+}
+
+
+// ---------------------------------------------------------------- ring-buffer (v2) layer
+
+bool rows_aligned16(const sink_rows_t* r, int es) {
+  return aligned16(r->data) && !((r->stride_b * es) & 15) && !((r->stride_h * es) & 15);
+}
+
+// Checks of sink_v2_place / sink_v2_decode_step; fills the kernel arguments.
+int32_t v2_args(const sink_kv_buffers_t* kv, const sink_rows_t* k_new, const sink_rows_t* v_new,
+                const sink_rows_t* region_keys, const int64_t* region_pos, int32_t R,
+                const sink_rows_t* region_out, int64_t* position, int64_t t_host, int32_t n_sink,
+                int32_t window, const double* inv_freq, int32_t rot_half, V2PlaceArgs& a) {
+  int32_t rc = check_kv(kv);
+  if (rc) return rc;
+  if (kv->k_dtype != kv->v_dtype) return SINK_EDTYPE;
+  if (n_sink < 0 || window < 1 || R < 0) return SINK_EINVAL;
+  const int64_t ring = int64_t(window) + 1;
+  if (ring + R > kv->slots) return SINK_EINVAL;
+  if (!position && t_host < 0) return SINK_EINVAL;
+  const int D = kv->head_dim, es = elem_size(kv->k_dtype);
+  std::memset(&a, 0, sizeof(a));
+  if ((k_new == nullptr) != (v_new == nullptr)) return SINK_EINVAL;
+  if (k_new) {
+    if ((rc = check_rows(k_new, kv->v_dtype, kv->batch, kv->heads_kv, 1))) return rc;
+    if ((rc = check_rows(v_new, kv->v_dtype, kv->batch, kv->heads_kv, 1))) return rc;
+    if (!rows_aligned16(k_new, es) || !rows_aligned16(v_new, es)) return SINK_ELAYOUT;
+    a.knew = static_cast<const char*>(k_new->data);
+    a.vnew = static_cast<const char*>(v_new->data);
+    a.kn_sb = k_new->stride_b;
+    a.kn_sh = k_new->stride_h;
+    a.vn_sb = v_new->stride_b;
+    a.vn_sh = v_new->stride_h;
+  }
+  a.kbuf = static_cast<char*>(kv->k);
+  a.vbuf = static_cast<char*>(kv->v);
+  a.k_sb = kv->k_stride_b;
+  a.k_sh = kv->k_stride_h;
+  a.v_sb = kv->v_stride_b;
+  a.v_sh = kv->v_stride_h;
+  if (R > 0) {
+    if (!region_keys || !region_keys->data || !region_pos || !inv_freq) return SINK_EINVAL;
+    if (region_keys->dtype != kv->k_dtype) return SINK_EDTYPE;
+    if (region_keys->heads != kv->heads_kv || region_keys->n < R) return SINK_EINVAL;
+    if (rot_half < 1 || 2 * rot_half > D) return SINK_EINVAL;
+    a.reg_k = static_cast<const char*>(region_keys->data);
+    a.rk_sb = region_keys->stride_b;
+    a.rk_sh = region_keys->stride_h;
+    a.rk_st = region_keys->stride_t;
+    if (region_out) {
+      if (!region_out->data) return SINK_EINVAL;
+      if (region_out->dtype != kv->k_dtype) return SINK_EDTYPE;
+      if (region_out->heads != kv->heads_kv || region_out->n < R) return SINK_EINVAL;
+      a.rout = static_cast<char*>(region_out->data);
+      a.ro_sb = region_out->stride_b;
+      a.ro_sh = region_out->stride_h;
+      a.ro_st = region_out->stride_t;
+    } else {
+      a.rout = static_cast<char*>(kv->k) + ring * D * es;
+      a.ro_sb = kv->k_stride_b;
+      a.ro_sh = kv->k_stride_h;
+      a.ro_st = D;
+    }
+  }
+  a.reg_pos = region_pos;
+  a.position = position;
+  a.t_host = t_host;
+  a.inv_freq = inv_freq;
+  a.n_sink = n_sink;
+  a.window = window;
+  a.ring = int(ring);
+  a.R = R;
+  a.rot_half = rot_half;
+  a.heads_kv = kv->heads_kv;
+  a.pairs = kv->batch * kv->heads_kv;
+  return SINK_OK;
+}
+
+template <typename T>
+int32_t launch_v2_place_t(int D, const V2PlaceArgs& a, int sms, cudaStream_t st) {
+  const int grid = a.pairs < sms * 8 ? a.pairs : sms * 8;
+  switch (D) {
+    case 64: return launch_dependent(sink_v2_place_kernel<T, 64>, dim3(grid), 0, st, a);
+    case 128: return launch_dependent(sink_v2_place_kernel<T, 128>, dim3(grid), 0, st, a);
+    case 256: return launch_dependent(sink_v2_place_kernel<T, 256>, dim3(grid), 0, st, a);
+    default: return SINK_EHEADDIM;
+  }
+}
+
+int32_t launch_v2_place(const sink_kv_buffers_t* kv, const V2PlaceArgs& a, int sms, cudaStream_t st) {
+  if (a.pairs < 1) return SINK_EINVAL;
+  switch (kv->k_dtype) {
+    case SINK_DTYPE_BF16: return launch_v2_place_t<__nv_bfloat16>(kv->head_dim, a, sms, st);
+    case SINK_DTYPE_F16: return launch_v2_place_t<__half>(kv->head_dim, a, sms, st);
+    case SINK_DTYPE_F32: return launch_v2_place_t<float>(kv->head_dim, a, sms, st);
+    default: return SINK_EDTYPE;
+  }
 }
 
 }  // namespace
@@ -409,39 +574,11 @@ int32_t sink_decode_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv,
                               void* workspace, size_t workspace_bytes, void* stream) {
   int32_t rc = check_kv(kv);
   if (rc) return rc;
-  if (!q || !q->data || !out) return SINK_EINVAL;
-  if (q->dtype != kv->v_dtype) return SINK_EDTYPE;
-  if (q->n != 1 || rows < 1 || rows > kv->slots) return SINK_EINVAL;
-  int dev = 0;
-  const int sms = device_sms(&dev);
-  if (sms <= 0) return SINK_EDEVICE;
   Plan pl;
-  rc = make_plan(SINK_OP_ATTEND, kv->batch, kv->heads_kv, q->heads, kv->head_dim, kv->k_dtype,
-                 kv->v_dtype, rows, 0, 1, 0, sms, pl);
-  if (rc) return rc;
-  if (!workspace || workspace_bytes < pl.total || !aligned16(workspace)) return SINK_EWORKSPACE;
-  StreamArgs A;
-  fill_common(A, kv, pl, static_cast<char*>(workspace));
-  A.group = q->heads / kv->heads_kv;
-  A.q = static_cast<const char*>(q->data);
-  A.q_sb = q->stride_b;
-  A.q_sh = q->stride_h;
-  A.out = static_cast<char*>(out);
-  A.o_sb = out_stride_b;
-  A.o_sh = out_stride_h;
-  A.window = 1;
-  A.row_begin = 0;
-  A.row_end = rows;
-  A.written_end = 0;
-  A.scale_log2 = scale * kLog2e;
-  A.mask = mask;
-  A.mask_sb = mask_stride_b;
-  const int pairs = kv->batch * kv->heads_kv;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if ((rc = dispatch_stream<true>(kv->k_dtype, kv->v_dtype, kv->head_dim, A.group, A, pl, pairs, st, dev)))
-    return rc;
-  if (pl.ns > 1) return launch_combine(kv->v_dtype, kv->head_dim, A, pairs, st);
-  return SINK_OK;
+  int dev = 0;
+  if ((rc = plan_attention(q, kv, rows, out, workspace, workspace_bytes, pl, &dev))) return rc;
+  return launch_attention(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
+                          out_stride_h, workspace, pl, dev, static_cast<cudaStream_t>(stream));
 }
 
 int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
@@ -509,6 +646,47 @@ int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k
     return rc;
   if (pl.ns > 1) return launch_combine(kv->v_dtype, kv->head_dim, A, pairs, st);
   return SINK_OK;
+}
+
+int32_t sink_v2_place(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
+                      const sink_rows_t* v_new, const sink_rows_t* region_keys,
+                      const int64_t* region_pos, int32_t region_len,
+                      const sink_rows_t* region_out, int64_t* position, int64_t t_host,
+                      int32_t n_sink, int32_t window, const double* inv_freq,
+                      int32_t rot_half, void* stream) {
+  V2PlaceArgs a;
+  const int32_t rc = v2_args(kv, k_new, v_new, region_keys, region_pos, region_len, region_out,
+                             position, t_host, n_sink, window, inv_freq, rot_half, a);
+  if (rc) return rc;
+  if (!k_new && region_len == 0 && !position) return SINK_OK;
+  int dev = 0;
+  const int sms = device_sms(&dev);
+  if (sms <= 0) return SINK_EDEVICE;
+  return launch_v2_place(kv, a, sms, static_cast<cudaStream_t>(stream));
+}
+
+int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
+                            const sink_rows_t* v_new, const sink_rows_t* region_keys,
+                            const int64_t* region_pos, int32_t region_len, int64_t* position,
+                            int32_t n_sink, int32_t window, const double* inv_freq,
+                            int32_t rot_half, const sink_rows_t* q, float scale,
+                            const uint8_t* mask, int64_t mask_stride_b, void* out,
+                            int64_t out_stride_b, int64_t out_stride_h, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (!k_new || !position) return SINK_EINVAL;
+  V2PlaceArgs a;
+  int32_t rc = v2_args(kv, k_new, v_new, region_keys, region_pos, region_len, nullptr, position,
+                       0, n_sink, window, inv_freq, rot_half, a);
+  if (rc) return rc;
+  const int32_t rows = window + 1 + region_len;
+  Plan pl;
+  int dev = 0;
+  if ((rc = plan_attention(q, kv, rows, out, workspace, workspace_bytes, pl, &dev))) return rc;
+  const int sms = device_sms(&dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = launch_v2_place(kv, a, sms, st))) return rc;
+  return launch_attention(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
+                          out_stride_h, workspace, pl, dev, st);
 }
 
 int32_t sink_read_status(void* workspace, void* stream, int32_t* status) {

@@ -49,6 +49,16 @@ def alg_bytes(slots: int, n_sink: int = N_SINK, hq: int = HQ, hkv: int = HKV, d:
     return 12 * w * e + 6 * n_sink * e + 10 * e + 4 * hq * d
 
 
+def alg_bytes_v2(slots: int, n_sink: int = N_SINK, hq: int = HQ, hkv: int = HKV, d: int = D) -> int:
+    """Algorithmic HBM bytes of one ring-buffer (v2) layer-step of one stream, K and V in bf16:
+    every window row read once (2 + 2 B per element), the new token read and stored in its
+    ring slot (8 B), the region's original keys and values read and its rotated keys stored
+    (6 B per region row element), q read and the output written.  The window is the same
+    slots - n_sink rows the v1 step moves."""
+    w, e = slots - n_sink, hkv * d
+    return 4 * w * e + 8 * e + 6 * n_sink * e + 4 * hq * d
+
+
 def inv_freq(d: int = D, theta: float = THETA) -> torch.Tensor:
     return 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
 
@@ -62,10 +72,10 @@ def hbm_peak() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic() -> dict:
-    """DRAM bytes per launch of the stream kernel from the committed ncu summary, if any
+def profiled_traffic(name: str = "sink_stream_kernel_traffic.txt") -> dict:
+    """DRAM bytes per launch of the dominant kernel from a committed ncu summary, if any
     (lines `traffic_bytes_per_launch: N` and `traffic_workload: ...`)."""
-    path = os.path.join(ROOT, "profiles", "sink_stream_kernel_traffic.txt")
+    path = os.path.join(ROOT, "profiles", name)
     out = {}
     try:
         with open(path) as f:
@@ -194,6 +204,57 @@ class OpBench:
         return self.k.numel() * 4 + self.v.numel() * 2
 
 
+class OpBenchV2:
+    """One ring-buffer (v2) layer of decode state for `batch` streams on one GPU in the steady
+    state: a ring of window + 1 slots holding keys rotated at their absolute positions, the
+    n_sink region rows (original keys at positions 0..n_sink-1), the device position far
+    from the origin, plus a small pool of per-step inputs.  A step is sink_v2_decode_step:
+    the place kernel (ring write, region rotation, position advance), split-K attention over
+    the window + 1 + n_sink rows and the split combine."""
+
+    POOL = 4
+
+    def __init__(self, batch: int, slots: int, device: torch.device, seed: int):
+        from attention_sinks_b200 import _lib
+        self.lib = _lib
+        self.batch, self.slots, self.device = batch, slots, device
+        self.window = slots - N_SINK
+        self.ring = self.window + 1
+        self.rows = self.ring + N_SINK
+        self.scale = D ** -0.5
+        bf = torch.bfloat16
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.k = torch.empty(batch, HKV, self.rows, D, dtype=bf, device=device)
+        self.v = torch.empty(batch, HKV, self.rows, D, dtype=bf, device=device)
+        for b in range(batch):  # key and value contents do not change the work: N(0, 1)
+            self.k[b] = torch.randn(HKV, self.rows, D, device=device, generator=g).to(bf)
+            self.v[b] = torch.randn(HKV, self.rows, D, device=device, generator=g).to(bf)
+        self.reg_k = torch.randn(batch, HKV, N_SINK, D, device=device, generator=g).to(bf)
+        self.reg_pos = torch.arange(N_SINK, device=device)
+        self.position = torch.tensor([10_000_000, 0], device=device)
+        self.inv = inv_freq().to(device, torch.float64)
+        self.q = [torch.randn(batch, HQ, 1, D, device=device, generator=g).to(bf) for _ in range(self.POOL)]
+        self.kn = [torch.randn(batch, HKV, 1, D, device=device, generator=g).to(bf) for _ in range(self.POOL)]
+        self.vn = [torch.randn(batch, HKV, 1, D, device=device, generator=g).to(bf) for _ in range(self.POOL)]
+        self.out = torch.empty(batch, 1, HQ, D, dtype=bf, device=device)
+        self.ws = _lib.Workspace()
+        sms = _lib.sm_count(device)
+        self.ws.get(_lib.workspace_bytes(_lib.OP_ATTEND, batch, HKV, HQ, D, bf, bf, self.rows, 0, 1, 0, sms), device)
+        self.plan = _lib.plan(_lib.OP_ATTEND, batch, HKV, HQ, D, bf, bf, self.rows, 0, 1, 0, sms)
+
+    def launches_per_step(self) -> int:
+        return 2 + (1 if self.plan["splits"] > 1 else 0)  # place, attention, split combine
+
+    def step(self, i: int) -> None:
+        j = i % self.POOL
+        self.lib.v2_decode_step(self.k, self.v, self.kn[j], self.vn[j], self.reg_k, self.reg_pos, N_SINK,
+                                self.position, N_SINK, self.window, self.inv, self.q[j], self.scale, self.out,
+                                self.ws)
+
+    def state_bytes(self) -> int:
+        return (self.k.numel() + self.v.numel()) * 2
+
+
 def flush_l2(buf: torch.Tensor, i: int) -> None:
     """Evict the state from L2 between timed steps: write one half of `buf` (2x L2), then
     read the other half, so L2 is left holding clean lines and the timed step does not
@@ -307,6 +368,74 @@ def cpu_baseline(slots: int, seconds: float = 15.0) -> dict:
                       f"SinkLayer.update (PyTorch path) + SDPA, torch threads={threads}"}
 
 
+def run_e2e_v2(bench: OpBenchV2, steps: int, warmup: int) -> tuple[float, int, int]:
+    """ms/step of the ring-buffer step through the public API with host buffers: per step the
+    new q/k/v are copied from pinned host memory, SinkLayerV2.update + the registered
+    attention backend run the fused step, and the output is copied to pinned host memory."""
+    from attention_sinks_b200 import SinkLayerV2
+    from attention_sinks_b200.decode_attention import decode_attention_forward
+    dev = bench.device
+    layer = SinkLayerV2(N_SINK, bench.window, inv_freq(), fused=True)
+    layer.update(bench.k[:, :, :bench.slots], bench.v[:, :, :bench.slots])  # one chunk fills the cache
+    assert layer.t == bench.slots and layer.in_cache_length() == bench.slots
+    torch.cuda.empty_cache()
+    pool = OpBenchV2.POOL
+    hq = [bench.q[j].cpu().pin_memory() for j in range(pool)]
+    hk = [bench.kn[j].cpu().pin_memory() for j in range(pool)]
+    hv = [bench.vn[j].cpu().pin_memory() for j in range(pool)]
+    hout = [torch.empty(bench.out.shape, dtype=bench.out.dtype).pin_memory() for _ in range(pool)]
+    module = _Module()
+
+    def step(i):
+        j = i % pool
+        q = hq[j].to(dev, non_blocking=True)
+        k = hk[j].to(dev, non_blocking=True)
+        v = hv[j].to(dev, non_blocking=True)
+        keys, values = layer.update(k, v)
+        o, _ = decode_attention_forward(module, q, keys, values, None, scaling=bench.scale)
+        hout[j].copy_(o, non_blocking=True)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        step(i)
+    end.record()
+    end.synchronize()
+    h2d = (hq[0].numel() + hk[0].numel() + hv[0].numel()) * 2
+    d2h = hout[0].numel() * 2
+    del layer
+    return start.elapsed_time(end) / steps, h2d, d2h
+
+
+def cpu_baseline_v2(slots: int, seconds: float = 15.0) -> dict:
+    """The reference's CPU path for the ring-buffer layer (oracle port: SinkLayerV2.update +
+    SDPA attention) on this host's cores, one stream of the workload."""
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    layer = oracle.make_prefilled_cache_v2(1, HKV, D, slots, N_SINK, inv_freq(), seed=0)
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, HQ, 1, D, generator=g).bfloat16()
+    kn = torch.randn(1, HKV, 1, D, generator=g).bfloat16()
+    vn = torch.randn(1, HKV, 1, D, generator=g).bfloat16()
+    oracle.reference_cpu_step_v2(layer, q, kn, vn, D ** -0.5)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        oracle.reference_cpu_step_v2(layer, q, kn, vn, D ** -0.5)
+        n += 1
+        el = time.perf_counter() - t0
+        if el > seconds or n >= 1000:
+            break
+    ms = el * 1e3 / n
+    return {"value": round(alg_bytes_v2(slots) / (ms * 1e-3) / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port", "ms_per_step": round(ms, 3),
+            "sample": f"1 stream x {slots} slots (of the per-GPU workload), {n} steps, oracle port of "
+                      f"SinkLayerV2.update (ring step) + SDPA, torch threads={threads}"}
+
+
 def time_graph(bench: OpBench, steps: int, flush: torch.Tensor | None) -> float:
     """Mean ms per step of one captured step replayed from a CUDA graph (how StreamRunner
     runs it: no host launch cost inside the step).  With `flush`, L2 is overwritten between
@@ -343,18 +472,19 @@ def time_graph(bench: OpBench, steps: int, flush: torch.Tensor | None) -> float:
     return total / steps
 
 
-def sweep(device: torch.device, flush: torch.Tensor) -> dict:
+def sweep(device: torch.device, flush: torch.Tensor, cls=None, alg=None) -> dict:
     """µs per layer-step and GB/s over the op-bench grid (slots x streams), 1 GPU, from
     CUDA-graph replays (L2 flushed between replays when the state is smaller than 2x L2)."""
+    cls, alg = cls or OpBench, alg or alg_bytes
     out = {}
     for slots in (256, 1024, 4096, 32768):
         for batch in (1, 8, 64):
-            b = OpBench(batch, slots, device, seed=slots + batch)
+            b = cls(batch, slots, device, seed=slots + batch)
             small = b.state_bytes() < 2 * L2_BYTES
-            steps = 50 if small else max(10, min(200, int(2e9 / (alg_bytes(slots) * batch))))
+            steps = 50 if small else max(10, min(200, int(2e9 / (alg(slots) * batch))))
             ms = time_graph(b, steps, flush if small else None)
             out[f"S{slots}_B{batch}"] = {"us_per_layer": round(ms * 1e3, 2),
-                                        "GB_s": round(alg_bytes(slots) * batch / (ms * 1e-3) / 1e9, 1),
+                                        "GB_s": round(alg(slots) * batch / (ms * 1e-3) / 1e9, 1),
                                         "l2_flushed": small}
             del b
             torch.cuda.empty_cache()
@@ -481,6 +611,28 @@ def run_model(args, workload: str) -> None:
     streams.shutdown()
 
 
+def op_kinds() -> dict:
+    """The two cache layouts' layer-step benchmarks."""
+    return {
+        "v1": dict(cls=OpBench, alg=alg_bytes, e2e=run_e2e, cpu=cpu_baseline, traffic="sink_stream_kernel_traffic.txt",
+                   workload=f"sink-cache fused decode layer-step: evict 1 + rerotate -1 + append + GQA decode "
+                            f"attention, Qwen3-0.6B layer shape (Hq {HQ}, Hkv {HKV}, head_dim {D})",
+                   key_dtype="fp32", dtype="f32",
+                   kernel="sink_stream_kernel<float, bf16, 128, 2, true> (timed with its halo pre-pass and "
+                          "split-combine launches: the whole fused step)",
+                   api="SinkLayer.update + decode_attention_forward (fused step)"),
+        "v2": dict(cls=OpBenchV2, alg=alg_bytes_v2, e2e=run_e2e_v2, cpu=cpu_baseline_v2,
+                   traffic="sink_v2_decode_step_traffic.txt",
+                   workload=f"ring-buffer (v2) decode layer-step: ring write + region rotation (fp64 angles) + "
+                            f"GQA decode attention over window + 1 + n_sink rows, Qwen3-0.6B layer shape "
+                            f"(Hq {HQ}, Hkv {HKV}, head_dim {D})",
+                   key_dtype="bf16", dtype="bf16",
+                   kernel="sink_stream_kernel<bf16, bf16, 128, 2, true> attend-only (timed with the place "
+                          "kernel and split combine: the whole v2 step)",
+                   api="SinkLayerV2.update + decode_attention_forward (fused step)"),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -489,10 +641,12 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--slots", type=int, default=32768)
     ap.add_argument("--streams", type=int, default=64, help="streams per GPU")
+    ap.add_argument("--cache", choices=("v1", "v2"), default="v1",
+                    help="v1: SinkCache fused step (default); v2: SinkCacheV2 ring-buffer step")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", default="op", choices=["op"] + sorted(model_configs()),
-                    help="op: the fused layer-step (default); otherwise a model-level streamed run")
+                    help="op: the layer-step (default); otherwise a model-level streamed run")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -500,12 +654,14 @@ def main():
         return run_model(args, args.workload)
 
     from attention_sinks_b200 import streams
+    kind = op_kinds()[args.cache]
+    alg = kind["alg"]
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
-    config = {"workload": f"sink-cache fused decode layer-step: evict 1 + rerotate -1 + append + GQA decode "
-                          f"attention, Qwen3-0.6B layer shape (Hq {HQ}, Hkv {HKV}, head_dim {D})",
+    config = {"workload": kind["workload"], "cache": args.cache,
               "slots": args.slots, "n_sink": N_SINK, "window": args.slots - N_SINK,
               "streams_per_gpu": args.streams, "global_streams": args.streams * max(world_env, 1),
-              "key_dtype": "fp32", "value_dtype": "bf16", "parallelism": f"streams x{max(world_env, 1)} (no collective)",
+              "key_dtype": kind["key_dtype"], "value_dtype": "bf16",
+              "parallelism": f"streams x{max(world_env, 1)} (no collective)",
               "l2": "state per GPU larger than L2: no flush between steps"}
 
     if args.impl == "reference":
@@ -514,11 +670,11 @@ def main():
             return
         steps = max(1, args.steps)
         seconds = min(120.0, 0.3 * steps + 5)
-        cb = cpu_baseline(args.slots, seconds=seconds)
+        cb = kind["cpu"](args.slots, seconds=seconds)
         v = cb["value"] * 1.0
         line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_step"],
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": kind["dtype"],
                 "data": "synthetic", "config": config, "cpu_baseline": cb,
                 "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -532,7 +688,7 @@ def main():
     from attention_sinks_b200 import build
     build.build()  # no-op when the shipped library is current
 
-    bench = OpBench(args.streams, args.slots, device, seed=1000 + rank)
+    bench = kind["cls"](args.streams, args.slots, device, seed=1000 + rank)
     small = bench.state_bytes() < 2 * L2_BYTES
     if small:
         config["l2"] = ("state smaller than 2x L2: between steps 256 MB written then 256 MB read (L2 left "
@@ -554,17 +710,17 @@ def main():
     if status:
         raise SystemExit(f"kernel status word {status}: a bounded wait ran out")
 
-    e2e_ms, h2d, d2h = run_e2e(bench, args.steps, args.warmup)
+    e2e_ms, h2d, d2h = kind["e2e"](bench, args.steps, args.warmup)
     streams.barrier()
     e2e_max = streams.reduce_max(e2e_ms)
 
-    bytes_step = alg_bytes(args.slots) * args.streams
+    bytes_step = alg(args.slots) * args.streams
     total_bytes = bytes_step * world
     value = total_bytes / (ms_max * 1e-3) / 1e9
     e2e_value = total_bytes / (e2e_max * 1e-3) / 1e9
     peak, peak_kind = hbm_peak()
     per_gpu = bytes_step / (ms * 1e-3) / 1e9
-    prof = profiled_traffic()
+    prof = profiled_traffic(kind["traffic"])
     traffic = None
     if "traffic_bytes_per_launch" in prof:
         try:
@@ -573,9 +729,7 @@ def main():
             traffic = None
     roofline = {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(per_gpu / peak, 4), "traffic": traffic, "peak_source": peak_kind,
-                "kernel": "sink_stream_kernel<float, bf16, 128, 2, true> (timed with its halo pre-pass and "
-                          "split-combine launches: the whole fused step)",
-                "algorithmic_bytes_per_launch": bytes_step}
+                "kernel": kind["kernel"], "algorithmic_bytes_per_launch": bytes_step}
     if "traffic_workload" in prof:
         roofline["traffic_workload"] = prof["traffic_workload"]
 
@@ -587,19 +741,18 @@ def main():
             flush = torch.empty(512 * 2 ** 20, dtype=torch.uint8, device=device)
             del bench
             torch.cuda.empty_cache()
-            extra["sweep"] = sweep(device, flush)
+            extra["sweep"] = sweep(device, flush, kind["cls"], alg)
             del flush
         if not args.no_cpu:
-            extra["cpu_baseline"] = cpu_baseline(args.slots)
+            extra["cpu_baseline"] = kind["cpu"](args.slots)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
                 "us_per_layer": round(ms_max * 1e3, 2), "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "vs_baseline": None, "dtype": kind["dtype"], "data": "synthetic", "config": config,
                 "roofline": roofline,
                 "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_max, 4),
-                        "api": "SinkLayer.update + decode_attention_forward (fused step)"},
+                        "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_max, 4), "api": kind["api"]},
                 "gpu_launches": launches, "clocks": clk, "plan": plan}
         line.update(extra)
         print(json.dumps(line), flush=True)

@@ -181,6 +181,56 @@ int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k
 /* Copy the workspace status word to *status (synchronises `stream`) and clear it. */
 int32_t sink_read_status(void* workspace, void* stream, int32_t* status);
 
+/*
+ * Ring-buffer cache (SinkLayerV2, src/sinkcache/cache_v2.py:59-248).  Window keys stay at the
+ * rotation the model gave them (absolute positions); only the region -- the sinks and any
+ * pinned tokens -- is re-rotated, from stored originals, to sit just before the window.
+ * The layer's buffers are a ring of window + 1 slots followed by the region slots:
+ *   kv: [batch, heads_kv, window + 1 + region_cap, head_dim], K and V in the model dtype
+ * (k_dtype == v_dtype).  The token at absolute position p >= n_sink sits in ring slot
+ * (p - n_sink) mod (window + 1).
+ *
+ * Place step:
+ *   - (k_new, v_new) [batch, heads_kv, 1, head_dim], optional (both or neither): written to
+ *     ring slot (t - n_sink) mod (window + 1);
+ *   - region_keys [batch, heads_kv, >= R, head_dim], rows 0..R-1 at their original rotations,
+ *     region_pos (device int64 [>= R]) their original positions: row j is rotated to
+ *     position ws - R + j, ws = max(min(t, n_sink), t - window), into region_out rows
+ *     0..R-1 (NULL: the kv rows window+1 .. window+R).  Angles in fp64, cos/sin rounded to
+ *     fp32, fp32 math, one rounding to k_dtype; inv_freq (device fp64 [rot_half]) covers the
+ *     first 2 * rot_half dims (HF half-split layout), the rest pass through;
+ *   - position (optional): device int64[2] = {t, 0}.  t is read on the device and advanced
+ *     by one when the step ends, so a CUDA graph of the step serves every later token; the
+ *     second word is an arrival counter that must be 0 between calls.  NULL: t = t_host,
+ *     nothing advanced.
+ * Replaces the device work of SinkLayerV2._decode_step (cache_v2.py:171-176: the slot
+ * index_copy_, the region copy of _rotate_region (:101-116) and _t_dev.add_(1)), and
+ * _rotate_region alone (region_out, no new token) for _general_step / kept() (:192, :234).
+ */
+int32_t sink_v2_place(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
+                      const sink_rows_t* v_new, const sink_rows_t* region_keys,
+                      const int64_t* region_pos, int32_t region_len,
+                      const sink_rows_t* region_out, int64_t* position, int64_t t_host,
+                      int32_t n_sink, int32_t window, const double* inv_freq,
+                      int32_t rot_half, void* stream);
+
+/*
+ * One steady-state decode step of a ring-buffer layer fused with its attention: the place
+ * step with (k_new, v_new) and `position`, then decode attention of q [batch, heads_q, 1,
+ * head_dim] over the window + 1 + R rows (ring, then region) -- as sink_decode_attention,
+ * with its mask convention over those rows.  Workspace: sink_workspace_bytes(SINK_OP_ATTEND,
+ * ..., rows = window + 1 + R, ...).  Replaces SinkLayerV2._decode_step (cache_v2.py:167-181)
+ * followed by decode_attention_forward over the views it returns (decode_attention.py:136-143).
+ */
+int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
+                            const sink_rows_t* v_new, const sink_rows_t* region_keys,
+                            const int64_t* region_pos, int32_t region_len, int64_t* position,
+                            int32_t n_sink, int32_t window, const double* inv_freq,
+                            int32_t rot_half, const sink_rows_t* q, float scale,
+                            const uint8_t* mask, int64_t mask_stride_b, void* out,
+                            int64_t out_stride_b, int64_t out_stride_h, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* Size of the static device scratch behind sink_decode_attention_noalloc: 16 MiB. */
 #define SINK_NOALLOC_SCRATCH_BYTES (16u << 20)
 

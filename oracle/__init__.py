@@ -10,5 +10,8 @@ from .sink_oracle import (OracleSinkLayer, apply_rope, decode_attention, decode_
                           make_prefilled_cache, rerotate, rerotate_fast, rope_cos_sin,
                           rotation_table)
 
-__all__ = ["OracleSinkLayer", "apply_rope", "decode_attention", "decode_step", "make_prefilled_cache", "reference_cpu_attention", "reference_cpu_step",
+from .sink_oracle_v2 import OracleSinkLayerV2, make_prefilled_cache_v2, reference_cpu_step_v2, region_rotation
+
+__all__ = ["OracleSinkLayerV2", "make_prefilled_cache_v2", "reference_cpu_step_v2", "region_rotation",
+           "OracleSinkLayer", "apply_rope", "decode_attention", "decode_step", "make_prefilled_cache", "reference_cpu_attention", "reference_cpu_step",
            "rerotate", "rerotate_fast", "rope_cos_sin", "rotation_table"]

@@ -144,3 +144,38 @@ def stream_nll(model, ids, cache, prefill=16, step=None):
         logits = step(ids[:, t:t + 1])[:, -1]
         nll.append(F.cross_entropy(logits.float(), ids[:, t + 1]))
     return torch.stack(nll).float().cpu(), logits[0].float().cpu()
+
+
+# ------------------------------------------------------------------ ring-buffer (v2) layer
+
+V2_CASES = [
+    dict(name="v2_s4_w60_bf16", n_sink=4, window=60, dtype="bf16", plan=[16] + [1] * 150),
+    dict(name="v2_s0_w60_bf16", n_sink=0, window=60, dtype="bf16", plan=[16] + [1] * 100),
+    dict(name="v2_s1_w60_fp32", n_sink=1, window=60, dtype="fp32", plan=[16] + [1] * 100),
+    dict(name="v2_pins", n_sink=4, window=60, dtype="bf16", pins=[(20, 30), (100, 105)], max_pinned=32,
+         plan=[16] + [1] * 84 + [40] + [1] * 160),
+    dict(name="v2_pin_budget", n_sink=4, window=60, dtype="bf16", pins=[(10, 16), (30, 36)], max_pinned=8,
+         plan=[16] + [1] * 183),
+    dict(name="v2_chunks", n_sink=4, window=60, dtype="bf16", plan=[200, 1, 1, 37, 90, 1, 1, 69]),
+    dict(name="v2_partial_rot", n_sink=4, window=30, dtype="bf16", rot=64, plan=[8] + [1] * 60),
+]
+V2_ROTATION_WS = [64, 2_000_000, 50_000_000]
+
+
+def v2_inputs(n_tokens, dtype_name, rot=128, batch=2, heads=2, d=128, seed=11):
+    """Keys as a model writes them (rotated at their absolute positions, first `rot` dims),
+    values N(0,1); [batch, heads, n_tokens, d] in the case dtype."""
+    g = torch.Generator().manual_seed(seed)
+    dtype = DTYPES[dtype_name]
+    inv = inv_freq(rot, 1e6)
+    raw = torch.randn(batch, heads, n_tokens, d, generator=g) * 3
+    k = torch.cat((rotated_keys(raw[..., :rot], torch.arange(n_tokens), inv), raw[..., rot:]), -1)
+    v = torch.randn(batch, heads, n_tokens, d, generator=g)
+    return k.to(dtype), v.to(dtype), inv
+
+
+def v2_rotation_inputs(seed=12):
+    """Region keys at their original rotations and far-apart original positions."""
+    g = torch.Generator().manual_seed(seed)
+    reg_k = (torch.randn(1, 8, 6, 128, generator=g) * 30).to(torch.bfloat16)
+    return reg_k, [0, 1, 2, 3, 500_000, 1_200_000], inv_freq(128, 1e6)

@@ -40,10 +40,24 @@ def load_reference(path: str):
     sys.path.insert(0, path)
     import sinkcache.cache as rc  # noqa: F401
     from sinkcache.cache import SinkLayer
-    SinkLayer.get_max_cache_shape = SinkLayer.get_max_length
-    SinkLayer.__abstractmethods__ = frozenset()
+    from sinkcache.cache_v2 import SinkLayerV2
+    for cls in (SinkLayer, SinkLayerV2):
+        cls.get_max_cache_shape = cls.get_max_length
+        cls.__abstractmethods__ = frozenset()
     import sinkcache
     return sinkcache
+
+
+def v2_causal_chunk_mask(layer_cls):
+    """Harness shim for the v2 layer under the installed transformers 5.5.0, which places a
+    chunk's queries at get_seq_length() (the absolute position, for a v2 layer) when it builds
+    the causal mask: returning kv_offset = t - in_cache_length makes chunk query i see chunk
+    keys 0..i and every cached key -- the causal mask the reference gets under the
+    transformers it pins (its SinkCacheV2.get_query_offset).  Decode steps are unaffected."""
+    def get_mask_sizes(self, query_length):
+        n = self.in_cache_length()
+        return n + query_length, self.t - n
+    layer_cls.get_mask_sizes = get_mask_sizes
 
 
 def evict_cases(ref, out, arrays):
@@ -178,6 +192,69 @@ def llama_stream_case(ref, out, arrays):
     arrays["llama_stream/last_logits"] = logits.float().numpy()
 
 
+def v2_layer_cases(ref, out, arrays):
+    """The reference SinkLayerV2 driven directly with seeded K/V chunks (cache_v2.py:159-208):
+    after every segment of the plan, the logical cache (kept(): keys, values, positions) and
+    the bookkeeping; the K/V the last step returned."""
+    from sinkcache.cache_v2 import SinkLayerV2
+    res = {}
+    for spec in cases.V2_CASES:
+        rot = spec.get("rot", 128)
+        total = sum(spec["plan"])
+        k, v, inv = cases.v2_inputs(total, spec["dtype"], rot)
+        pinned = set()
+        for a, b in spec.get("pins", []):
+            pinned.update(range(a, b))
+        layer = SinkLayerV2(spec["n_sink"], spec["window"], inv, spec.get("max_pinned", 0), pinned)
+        t, marks = 0, []
+        segments = []  # (start, n) runs of equal-size steps
+        for n in spec["plan"]:
+            if segments and n == 1 and segments[-1][1] == 1:
+                segments[-1][2] += 1
+            else:
+                segments.append([t, n, 1])
+            t += n
+        t = 0
+        for start, n, reps in segments:
+            for _ in range(reps):
+                keys, values = layer.update(k[:, :, t:t + n], v[:, :, t:t + n])
+                t += n
+            kk, vv, pos = layer.kept()
+            marks.append({"t": layer.t, "kept_k": digest(kk), "kept_v": digest(vv), "positions": pos,
+                          "region_pos": list(layer.region_pos), "moved_upto": layer.moved_upto,
+                          "pins_dropped": layer.pins_dropped, "in_cache": layer.in_cache_length(),
+                          "step_k": digest(keys), "step_v": digest(values),
+                          "step_rows": int(keys.shape[-2])})
+        res[spec["name"]] = {"in_k": digest(k), "in_v": digest(v), "marks": marks}
+        arrays[spec["name"] + "/kept_k_rowsum"] = kk.double().sum(-1).numpy()
+    # the region rotation alone, far from the origin (fp64 angles): _rotate_region(ws)
+    reg_k, reg_pos, inv = cases.v2_rotation_inputs()
+    layer = SinkLayerV2(4, 60, inv, max_pinned=2)
+    layer.lazy_initialization(reg_k[:, :, :1], reg_k[:, :, :1])
+    layer._reg_k[:, :, :6] = reg_k
+    layer._reg_pos[:6] = torch.tensor(reg_pos)
+    layer.region_pos = list(reg_pos)
+    rot = {"in_k": digest(reg_k)}
+    for ws in cases.V2_ROTATION_WS:
+        rot[f"ws_{ws}"] = digest(layer._rotate_region(ws))
+    res["rotation"] = rot
+    out["v2"] = res
+
+
+def v2_stream_case(ref, out, arrays):
+    """Tiny random-init Qwen3 (fp32) streamed through the reference SinkCacheV2(4, 60): prefill
+    16, then one token at a time; per-token NLL and bookkeeping."""
+    from sinkcache.cache_v2 import SinkCacheV2, SinkLayerV2
+    v2_causal_chunk_mask(SinkLayerV2)
+    model, ids = cases.tiny_qwen3(torch.float32)
+    cache = SinkCacheV2.from_model(model, n_sink=4, window=60)
+    nll, logits = cases.stream_nll(model, ids, cache, prefill=16)
+    out["v2_stream"] = {"tokens_seen": cache.tokens_seen, "tokens_evicted": cache.tokens_evicted,
+                        "region_size": cache.region_size, "mean_nll": float(nll.mean()), "ids": digest(ids)}
+    arrays["v2_stream/nll"] = nll.numpy()
+    arrays["v2_stream/last_logits"] = logits.numpy()
+
+
 def inv_freq_case(ref, out, arrays):
     """find_inv_freq on a Llama-3.2-1B-shaped config with llama3 rope scaling."""
     from sinkcache.cache import find_inv_freq
@@ -204,6 +281,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference/src")
     ap.add_argument("--config1", type=int, default=0, help="also stream N steps of random-init Qwen3-0.6B")
+    ap.add_argument("--only", default="", help="comma-separated case functions to regenerate (default: all)")
     args = ap.parse_args()
     ref = load_reference(args.reference)
     json_path = os.path.join(HERE, "golden.json")
@@ -212,8 +290,11 @@ def main():
     arrays = dict(np.load(npz_path)) if os.path.exists(npz_path) else {}
     out["meta"] = {"torch": torch.__version__, "reference": "buttaRahul/Attention_sinks src/sinkcache",
                    "transformers": __import__("transformers").__version__}
+    ap_only = args.only.split(",") if args.only else None
     for fn in (evict_cases, rerotate_cases, attention_cases, step_cases, stream_case, llama_stream_case,
-               inv_freq_case):
+               inv_freq_case, v2_layer_cases, v2_stream_case):
+        if ap_only and fn.__name__ not in ap_only:
+            continue
         t0 = time.time()
         fn(ref, out, arrays)
         print(f"{fn.__name__}: {time.time() - t0:.1f}s", flush=True)

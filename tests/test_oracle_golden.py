@@ -129,3 +129,59 @@ def test_find_inv_freq_llama3_scaling(golden_arrays):
     np.testing.assert_array_equal(got, golden_arrays["llama3_inv_freq"])
     plain = cases.inv_freq(64, 5e5).numpy()
     assert not np.array_equal(got, plain)  # the scaling changed the low frequencies
+
+
+# ------------------------------------------------------------------ ring-buffer (v2) layer
+
+
+def drive_v2(layer, spec, k, v):
+    """Feed the plan's chunks; after each run of equal steps, yield (keys, values) of the
+    last step (the segments make_golden.py records)."""
+    t, segments = 0, []
+    for n in spec["plan"]:
+        if segments and n == 1 and segments[-1][1] == 1:
+            segments[-1][2] += 1
+        else:
+            segments.append([t, n, 1])
+        t += n
+    t = 0
+    for _start, n, reps in segments:
+        for _ in range(reps):
+            keys, values = layer.update(k[:, :, t:t + n], v[:, :, t:t + n])
+            t += n
+        yield keys, values
+
+
+def v2_pinned(spec):
+    pinned = set()
+    for a, b in spec.get("pins", []):
+        pinned.update(range(a, b))
+    return pinned
+
+
+@pytest.mark.parametrize("spec", cases.V2_CASES, ids=lambda s: s["name"])
+def test_oracle_v2_layer_matches_reference(spec, golden):
+    """cache_v2.py:59-248 restated: ring slots, region rotation with fp64 angles, pins moving
+    into the region and the pin budget -- every checkpoint bit-identical to the reference."""
+    want = golden["v2"][spec["name"]]
+    k, v, inv = cases.v2_inputs(sum(spec["plan"]), spec["dtype"], spec.get("rot", 128))
+    _inputs_match(want, in_k=k, in_v=v)
+    layer = oracle.OracleSinkLayerV2(spec["n_sink"], spec["window"], inv, spec.get("max_pinned", 0),
+                                     v2_pinned(spec))
+    for (keys, values), mark in zip(drive_v2(layer, spec, k, v), want["marks"], strict=True):
+        kk, vv, pos = layer.kept()
+        assert layer.t == mark["t"] and pos == mark["positions"]
+        assert layer.region_pos == mark["region_pos"] and layer.pins_dropped == mark["pins_dropped"]
+        assert layer.moved_upto == mark["moved_upto"] and layer.in_cache_length() == mark["in_cache"]
+        assert keys.shape[-2] == mark["step_rows"]
+        assert digest(vv) == mark["kept_v"] and digest(values) == mark["step_v"]
+        assert digest(kk) == mark["kept_k"] and digest(keys) == mark["step_k"]
+
+
+def test_oracle_v2_region_rotation_far_positions(golden):
+    """_rotate_region at window starts up to 5e7 (fp64 angles): bit-identical."""
+    want = golden["v2"]["rotation"]
+    reg_k, reg_pos, inv = cases.v2_rotation_inputs()
+    _inputs_match(want, in_k=reg_k)
+    for ws in cases.V2_ROTATION_WS:
+        assert digest(oracle.region_rotation(reg_k, reg_pos, ws, inv)) == want[f"ws_{ws}"]
