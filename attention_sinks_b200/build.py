@@ -6,6 +6,7 @@ The library exports the C ABI declared in include/sinkcache_b200.h.  It links th
 runtime statically, so it needs nothing at run time beyond the driver.
 """
 
+import glob
 import os
 import shutil
 import subprocess
@@ -15,11 +16,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 SOURCES = [os.path.join(CSRC, "sinkcache_b200.cu")]
-HEADERS = [
-    os.path.join(CSRC, "sink_common.cuh"),
-    os.path.join(CSRC, "sink_kernels.cuh"),
-    os.path.join(ROOT, "include", "sinkcache_b200.h"),
-]
+# every header the translation unit includes: a change to any of them rebuilds the library
+HEADERS = sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
 LIB = os.path.join(HERE, "lib", "libsinkcache_b200.so")
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

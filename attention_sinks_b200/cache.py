@@ -71,6 +71,7 @@ class SinkLayer(CacheLayerMixin):
         self.fused = fused
         self._rot: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
         self._kbuf = self._vbuf = None
+        self._kstore = self._vstore = None  # row storage the buffers view (see _alloc)
         self._pending = None        # (drop, k, v, append_row) of a deferred one-token step
         self._ws = workspace if workspace is not None else _lib.Workspace()
 
@@ -90,12 +91,25 @@ class SinkLayer(CacheLayerMixin):
         self.is_initialized = True
 
     def _alloc(self, like, slots):
+        """Make the K/V buffers `slots` rows long, keeping their first `length` rows (the
+        reference reallocates on every grow and shrink, cache.py:97-104, 142-143).  The
+        buffers are views of a row storage that is only replaced when a chunk needs more
+        rows than it has (rows copied once, then later chunks of that size fit) or when a
+        shrink back to capacity + 1 would leave more than twice the rows idle: the usual
+        chunk step grows and shrinks without copying the cache, and the buffer pointers of
+        a captured steady step stay valid."""
         b, h, _, d = like.shape
+        store = self._kstore.shape[-2] if self._kstore is not None else 0
+        small = slots == self.capacity + 1
+        if slots <= store and not (small and store > 2 * slots):
+            self._kbuf, self._vbuf = self._kstore[:, :, :slots], self._vstore[:, :, :slots]
+            return
         k = torch.empty(b, h, slots, d, dtype=self.key_dtype, device=self.device)
         v = torch.empty(b, h, slots, d, dtype=self.dtype, device=self.device)
         if self.length:
             k[:, :, :self.length] = self._kbuf[:, :, :self.length]
             v[:, :, :self.length] = self._vbuf[:, :, :self.length]
+        self._kstore, self._vstore = k, v
         self._kbuf, self._vbuf = k, v
         _BY_BUFFER[k.data_ptr()] = self
 
@@ -224,6 +238,7 @@ class SinkLayer(CacheLayerMixin):
         self.length = self.tokens_seen = self.tokens_evicted = 0
         self.keys = self.values = None
         self._kbuf = self._vbuf = None
+        self._kstore = self._vstore = None
         self._pending = None
         self.is_initialized = False
 

@@ -90,6 +90,11 @@ class SinkLayerV2(CacheLayerMixin):
     def _slot(self, p: int) -> int:
         return (p - self.n_sink) % self.ring
 
+    def _slots(self, lo: int, hi: int) -> torch.Tensor:
+        """Ring slots of positions [lo, hi) (all >= n_sink) as a device index tensor, computed
+        on the device (cache_v2.py:190, 202 build them as host lists)."""
+        return (torch.arange(lo, max(lo, hi), device=self.device) - self.n_sink) % self.ring
+
     def _window_start(self, t: int) -> int:
         return max(min(t, self.n_sink), t - self.window)
 
@@ -203,7 +208,7 @@ class SinkLayerV2(CacheLayerMixin):
         ws = self._window_start(t)
         R = len(self.region_pos)
         win = range(max(ws, self.n_sink), t)
-        slots = torch.tensor([self._slot(p) for p in win], dtype=torch.long, device=self.device)
+        slots = self._slots(win.start, win.stop)
         r = self.ring
         b, h, _, d = self._kbuf.shape
         keys = torch.empty(b, h, R + len(win) + q, d, dtype=self.dtype, device=self.device)
@@ -218,7 +223,7 @@ class SinkLayerV2(CacheLayerMixin):
         self._move_pins(t + q - self.window, chunk=(k, v, t))
         lo = max(self.n_sink, t + q - self.ring, t)
         if lo < t + q:
-            idx = torch.tensor([self._slot(p) for p in range(lo, t + q)], dtype=torch.long, device=self.device)
+            idx = self._slots(lo, t + q)
             self._kbuf.index_copy_(2, idx, k[:, :, lo - t:])
             self._vbuf.index_copy_(2, idx, v[:, :, lo - t:])
         self.t = t + q
@@ -258,7 +263,7 @@ class SinkLayerV2(CacheLayerMixin):
         ws = self._window_start(t)
         R = len(self.region_pos)
         win = list(range(max(ws, self.n_sink), t))
-        slots = torch.tensor([self._slot(p) for p in win], dtype=torch.long, device=self.device)
+        slots = self._slots(max(ws, self.n_sink), t)
         r = self.ring
         k = torch.cat((self._rotate_region(t), self._kbuf.index_select(2, slots)), -2)
         v = torch.cat((self._vbuf[:, :, r:r + R], self._vbuf.index_select(2, slots)), -2)

@@ -4,7 +4,10 @@
 #include <climits>
 #include <cstring>
 
+#include <cudaTypedefs.h>
+
 #include "../../include/sinkcache_b200.h"
+#include "sink_attend_tc.cuh"
 #include "sink_kernels.cuh"
 #include "sink_v2.cuh"
 
@@ -32,6 +35,7 @@ bool supported_types(int32_t kdt, int32_t vdt) {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Plan {
+  bool tc = false;  // attention on the tensor-core kernel (sink_attend_tc_kernel)
   int T = 0, S = 0, stage = 0, smem = 0, ctas_per_sm = 0;
   int ns = 1, rows_per_split = 0, halo_rows = 0;
   size_t off_o = 0, off_m = 0, off_l = 0, off_hk = 0, off_hv = 0, total = 256;
@@ -51,6 +55,21 @@ bool geometry(int D, int ks, int vs, Plan& pl) {
   return true;
 }
 
+// Attention over 16-bit K = V dtype with head_dim 128 runs on the tensor cores.
+bool tc_attention(int32_t op, int32_t kdt, int32_t vdt, int D) {
+  return op == SINK_OP_ATTEND && kdt == vdt && (kdt == SINK_DTYPE_BF16 || kdt == SINK_DTYPE_F16) &&
+         D == kTcD;
+}
+
+void geometry_tc(Plan& pl) {
+  pl.tc = true;
+  pl.T = kTcRows;
+  pl.S = kTcStages;
+  pl.stage = kTcStageBytes;
+  pl.smem = kTcSmemBytes;
+  pl.ctas_per_sm = 1;
+}
+
 // Split plan: every (batch, head) pair's rows cut into `ns` items of `tps` chunks, one CTA
 // each.  Two regimes, from measurements over the op-bench grid on B200:
 //   - a step whose pairs fit in one wave of CTAs with items of at most kMaxItemChunks
@@ -61,16 +80,20 @@ bool geometry(int D, int ks, int vs, Plan& pl) {
 constexpr long kMinItemChunks = 4;
 constexpr long kMaxItemChunks = 32;
 constexpr long kTargetWaves = 16;
+// The persistent tensor-core kernel streams its items back to back, so it wants more,
+// smaller items (about 64 per CTA) to even out the last round.
+constexpr long kTcTargetItemsPerCta = 64;
+constexpr long kTcMinItemChunks = 2;
 
-void choose_splits(int pairs, int rows, int T, int slots, Plan& pl) {
+void choose_splits(int pairs, int rows, int T, int slots, long target_waves, long min_chunks, Plan& pl) {
   const long tiles = (rows + T - 1) / T;
   const long total = long(pairs) * tiles;
   long ns;
   if (long(pairs) * ((tiles + kMaxItemChunks - 1) / kMaxItemChunks) <= slots) {
     ns = slots / pairs;
   } else {
-    long tps = (total + kTargetWaves * slots - 1) / (kTargetWaves * slots);
-    tps = tps < kMinItemChunks ? kMinItemChunks : (tps > kMaxItemChunks ? kMaxItemChunks : tps);
+    long tps = (total + target_waves * slots - 1) / (target_waves * slots);
+    tps = tps < min_chunks ? min_chunks : (tps > kMaxItemChunks ? kMaxItemChunks : tps);
     ns = (tiles + tps - 1) / tps;
   }
   if (ns > tiles) ns = tiles;
@@ -99,13 +122,17 @@ int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
     if (G > kMaxGroup) return SINK_EGROUP;
   }
   if (n_sink < 0 || window < 1 || drop < 0) return SINK_EINVAL;
+  if (tc_attention(op, kdt, vdt, D)) geometry_tc(pl);
   int nrows;
   if (op == SINK_OP_EVICT) nrows = window;
   else if (op == SINK_OP_ATTEND || op == SINK_OP_FUSED_STEP) nrows = rows;
   else return SINK_EINVAL;
   if (nrows < 1) return SINK_EINVAL;
   const int pairs = batch * heads_kv;
-  choose_splits(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, pl);
+  if (pl.tc)
+    choose_splits(pairs, nrows, pl.T, num_sms, kTcTargetItemsPerCta, kTcMinItemChunks, pl);
+  else
+    choose_splits(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, kTargetWaves, kMinItemChunks, pl);
   size_t off = 256;  // status word
   if (attend && pl.ns > 1) {
     const size_t parts = size_t(pairs) * pl.ns * G;
@@ -172,10 +199,11 @@ int32_t check_rows(const sink_rows_t* r, int32_t dtype, int32_t batch, int32_t h
 // predecessor in the stream finishes (every kernel here waits on the grid dependency before
 // touching memory), which hides the launch gap between the halo, stream and combine kernels.
 template <typename... Params, typename... Args>
-int32_t launch_dependent(void (*kern)(Params...), dim3 grid, int smem, cudaStream_t st, Args... args) {
+int32_t launch_dependent_n(void (*kern)(Params...), dim3 grid, int threads, int smem, cudaStream_t st,
+                           Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = size_t(smem);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -186,6 +214,11 @@ int32_t launch_dependent(void (*kern)(Params...), dim3 grid, int smem, cudaStrea
   const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, args...);
   if (err != cudaSuccess) return err;
   return cudaGetLastError();
+}
+
+template <typename... Params, typename... Args>
+int32_t launch_dependent(void (*kern)(Params...), dim3 grid, int smem, cudaStream_t st, Args... args) {
+  return launch_dependent_n(kern, grid, kThreads, smem, st, args...);
 }
 
 template <typename KT, typename VT, int D, int GMAX, bool ATTEND>
@@ -322,11 +355,148 @@ int32_t plan_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_
   return SINK_OK;
 }
 
-// Split-K decode attention over rows [0, rows): stream kernel in attend-only mode + combine.
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::atomic<void*> cached{nullptr};
+  void* fn = cached.load(std::memory_order_acquire);
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return nullptr;
+    cached.store(fn, std::memory_order_release);
+  }
+  return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+}
+
+// 4-D map over one cache buffer [B, Hkv, slots, 128] (innermost first), boxes of 64 columns
+// x 128 rows with 128-byte swizzle; rows past `slots` read as zeros.
+int32_t encode_cache_map(CUtensorMap* map, void* data, int32_t dtype, const sink_kv_buffers_t* kv,
+                         int64_t stride_b, int64_t stride_h) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return SINK_EDEVICE;
+  const int es = elem_size(dtype);
+  const cuuint64_t dims[4] = {cuuint64_t(kv->head_dim), cuuint64_t(kv->slots), cuuint64_t(kv->heads_kv),
+                              cuuint64_t(kv->batch)};
+  const cuuint64_t strides[3] = {cuuint64_t(kv->head_dim) * es, cuuint64_t(stride_h) * es,
+                                 cuuint64_t(stride_b) * es};
+  const cuuint32_t box[4] = {64, kTcRows, 1, 1};
+  const cuuint32_t unit[4] = {1, 1, 1, 1};
+  const CUresult r = encode(map, dtype == SINK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                            4, data, dims, strides, box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SINK_OK : SINK_ELAYOUT;
+}
+
+// Persistent launch: one CTA per SM at most, each walking items (split, pair).
+// 3-D map over the queries [B, Hq, 128] (the single token dimension dropped), boxes of 64
+// columns x G rows (one GQA group) with 128-byte swizzle.  Fails (then the kernel loads q
+// with plain loads) when q's rows are not 16-byte aligned.
+int32_t encode_query_map(CUtensorMap* map, const sink_rows_t* q, int batch, int G) {
+  if (!aligned16(q->data) || ((q->stride_b * 2) & 15) || ((q->stride_h * 2) & 15)) return SINK_ELAYOUT;
+  if (q->stride_h < kTcD || q->stride_b < 1) return SINK_ELAYOUT;
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return SINK_EDEVICE;
+  const cuuint64_t dims[3] = {cuuint64_t(kTcD), cuuint64_t(q->heads), cuuint64_t(batch)};
+  const cuuint64_t strides[2] = {cuuint64_t(q->stride_h) * 2, cuuint64_t(q->stride_b) * 2};
+  const cuuint32_t box[3] = {64, cuuint32_t(G), 1};
+  const cuuint32_t unit[3] = {1, 1, 1};
+  const CUresult r = encode(map, q->dtype == SINK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                            3, q->data, dims, strides, box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SINK_OK : SINK_ELAYOUT;
+}
+
+template <typename T, int GMAX>
+int32_t launch_tc_g(const TcArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev) {
+  auto kern = sink_attend_tc_kernel<T, GMAX>;
+  static std::atomic<uint64_t> configured{0};  // per instantiation: one bit per device
+  const uint64_t bit = uint64_t(1) << dev;
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    const cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
+    if (err != cudaSuccess) return err;
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const int sms = device_sms(&dev);
+  if (sms <= 0) return SINK_EDEVICE;
+  const long items = long(pl.ns) * pairs;
+  const int grid = int(items < sms ? items : sms);
+  return launch_dependent_n(kern, dim3(grid), kTcThreads, kTcSmemBytes, st, A);
+}
+
+template <typename T>
+int32_t launch_tc_t(int G, const TcArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev) {
+  if (G <= 1) return launch_tc_g<T, 1>(A, pl, pairs, st, dev);
+  if (G <= 2) return launch_tc_g<T, 2>(A, pl, pairs, st, dev);
+  if (G <= 4) return launch_tc_g<T, 4>(A, pl, pairs, st, dev);
+  return launch_tc_g<T, 8>(A, pl, pairs, st, dev);
+}
+
+int32_t launch_attention_tc(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows,
+                            float scale, const uint8_t* mask, int64_t mask_stride_b, void* out,
+                            int64_t out_stride_b, int64_t out_stride_h, void* workspace,
+                            const Plan& pl, int dev, cudaStream_t st) {
+  TcArgs A;
+  std::memset(&A, 0, sizeof(A));
+  int32_t rc = encode_cache_map(&A.kmap, kv->k, kv->k_dtype, kv, kv->k_stride_b, kv->k_stride_h);
+  if (rc) return rc;
+  if ((rc = encode_cache_map(&A.vmap, kv->v, kv->v_dtype, kv, kv->v_stride_b, kv->v_stride_h))) return rc;
+  char* ws = static_cast<char*>(workspace);
+  A.q = static_cast<const char*>(q->data);
+  A.q_sb = q->stride_b;
+  A.q_sh = q->stride_h;
+  A.q_async = encode_query_map(&A.qmap, q, kv->batch, A.group = q->heads / kv->heads_kv) == SINK_OK;
+  A.out = static_cast<char*>(out);
+  A.o_sb = out_stride_b;
+  A.o_sh = out_stride_h;
+  A.mask = mask;
+  A.mask_sb = mask_stride_b;
+  A.o_part = pl.off_o ? reinterpret_cast<float*>(ws + pl.off_o) : nullptr;
+  A.m_part = pl.off_m ? reinterpret_cast<float*>(ws + pl.off_m) : nullptr;
+  A.l_part = pl.off_l ? reinterpret_cast<float*>(ws + pl.off_l) : nullptr;
+  A.status = reinterpret_cast<int*>(ws);
+  A.heads_kv = kv->heads_kv;
+  A.group = q->heads / kv->heads_kv;
+  A.row_end = rows;
+  A.rows_per_split = pl.rows_per_split;
+  A.ns = pl.ns;
+  A.scale_log2 = scale * kLog2e;
+  const int pairs = kv->batch * kv->heads_kv;
+  A.pairs = pairs;
+  rc = kv->k_dtype == SINK_DTYPE_BF16 ? launch_tc_t<__nv_bfloat16>(A.group, A, pl, pairs, st, dev)
+                                      : launch_tc_t<__half>(A.group, A, pl, pairs, st, dev);
+  if (rc) return rc;
+  if (pl.ns > 1) {
+    StreamArgs C;
+    std::memset(&C, 0, sizeof(C));
+    C.o_part = A.o_part;
+    C.m_part = A.m_part;
+    C.l_part = A.l_part;
+    C.out = A.out;
+    C.o_sb = A.o_sb;
+    C.o_sh = A.o_sh;
+    C.heads_kv = A.heads_kv;
+    C.group = A.group;
+    C.ns = A.ns;
+    return launch_combine(kv->v_dtype, kv->head_dim, C, pairs, st);
+  }
+  return SINK_OK;
+}
+
+// Split-K decode attention over rows [0, rows): the tensor-core kernel for 16-bit K with
+// head_dim 128, else the stream kernel in attend-only mode; then the split combine.
 int32_t launch_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows,
                          float scale, const uint8_t* mask, int64_t mask_stride_b, void* out,
                          int64_t out_stride_b, int64_t out_stride_h, void* workspace,
                          const Plan& pl, int dev, cudaStream_t st) {
+  if (pl.tc)
+    return launch_attention_tc(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
+                               out_stride_h, workspace, pl, dev, st);
   int32_t rc;
   StreamArgs A;
   fill_common(A, kv, pl, static_cast<char*>(workspace));

@@ -491,6 +491,72 @@ def sweep(device: torch.device, flush: torch.Tensor, cls=None, alg=None) -> dict
     return out
 
 
+# ----------------------------------------------------------------------------- chunk steps
+
+
+def chunk_bench(args) -> None:
+    """The general (multi-token) step on a full cache, one layer of the op-bench shape: a
+    chunk of `n` tokens per stream through the public API -- SinkLayer.update (pending
+    eviction of the previous chunk with re-rotation by -n, append, buffer growth and shrink)
+    or SinkLayerV2.update (region rotation, window gather, ring stores) -- then the chunk's
+    attention through the registered backend (SDPA over the returned K/V, as the
+    reference).  Device-resident inputs, CUDA events around `steps` chunk steps."""
+    from attention_sinks_b200 import SinkLayer, SinkLayerV2, streams
+    from attention_sinks_b200.decode_attention import decode_attention_forward
+    rank, world, local = streams.init_from_env("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(7)
+    bf = torch.bfloat16
+    for cache in ("v1", "v2"):
+        for slots in (4096, 32768):
+            for n in (16, 128, 512):
+                b = 8
+                if cache == "v1":
+                    layer = SinkLayer(N_SINK, slots - N_SINK, inv_freq(), key_dtype=torch.float32, fused=True)
+                else:
+                    layer = SinkLayerV2(N_SINK, slots - N_SINK, inv_freq(), fused=True)
+                for r0 in range(0, slots, 4096):  # fill the cache
+                    r1 = min(r0 + 4096, slots)
+                    layer.update(torch.randn(b, HKV, r1 - r0, D, device=dev, generator=g).to(bf),
+                                 torch.randn(b, HKV, r1 - r0, D, device=dev, generator=g).to(bf))
+                pool = [(torch.randn(b, HQ, n, D, device=dev, generator=g).to(bf),
+                         torch.randn(b, HKV, n, D, device=dev, generator=g).to(bf),
+                         torch.randn(b, HKV, n, D, device=dev, generator=g).to(bf)) for _ in range(2)]
+                module = _Module()
+
+                def step(i):
+                    q, k, v = pool[i % 2]
+                    keys, values = layer.update(k, v)
+                    o, _ = decode_attention_forward(module, q, keys, values, None, scaling=D ** -0.5)
+                    return o
+
+                for i in range(3):
+                    step(i)
+                torch.cuda.synchronize()
+                steps = 20
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+                for i in range(steps):
+                    step(i)
+                end.record()
+                end.synchronize()
+                ms = start.elapsed_time(end) / steps
+                out[f"{cache}_S{slots}_n{n}"] = {"us_per_chunk_step": round(ms * 1e3, 1),
+                                                "tokens_per_s_per_layer": round(b * n / (ms * 1e-3), 0)}
+                del layer, pool
+                torch.cuda.empty_cache()
+    if rank == 0:
+        line = {"metric": "chunk step µs/layer (general path)", "value": None, "unit": "us", "n_gpus": world,
+                "steps": 20, "warmup": 3, "higher_is_better": False, "dtype": "bf16 model / fp32 K (v1), bf16 K (v2)",
+                "data": "synthetic", "config": {"workload": "chunk steps on a full cache, 8 streams, Qwen3-0.6B "
+                                                             "layer shape", "n_sink": N_SINK},
+                "chunks": out}
+        print(json.dumps(line), flush=True)
+    streams.shutdown()
+
+
 # ----------------------------------------------------------------------------- model workloads
 
 
@@ -526,13 +592,14 @@ def model_configs():
 
 class ModelBench:
     """One model replica and `streams` sink caches on one GPU, filled to the steady state
-    (n_sink + window kept rows + one pending) through SinkLayer.update with synthetic K/V,
-    then streamed one token per step under the CUDA-graph StreamRunner."""
+    (v1: n_sink + window kept rows + one pending; v2: n_sink + window tokens seen) through
+    the layers' update with synthetic K/V, then streamed one token per step under the
+    CUDA-graph StreamRunner."""
 
-    def __init__(self, spec: dict, streams_: int, device: torch.device, seed: int):
+    def __init__(self, spec: dict, streams_: int, device: torch.device, seed: int, cache: str = "v1"):
         from transformers import AutoModelForCausalLM
 
-        from attention_sinks_b200 import SinkCache, StreamRunner, register
+        from attention_sinks_b200 import SinkCache, SinkCacheV2, StreamRunner, register
         name = register()
         cfg = spec["cfg"]()
         torch.manual_seed(seed)
@@ -540,9 +607,10 @@ class ModelBench:
             self.model = AutoModelForCausalLM.from_config(cfg, attn_implementation=name,
                                                           dtype=torch.bfloat16).eval()
         self.cfg, self.batch, self.device = cfg, streams_, device
-        self.cache = SinkCache.from_model(self.model, n_sink=spec["n_sink"], window=spec["window"])
+        cls = SinkCacheV2 if cache == "v2" else SinkCache
+        self.cache = cls.from_model(self.model, n_sink=spec["n_sink"], window=spec["window"])
         hkv, d = cfg.num_key_value_heads, cfg.head_dim
-        rows = spec["n_sink"] + spec["window"] + 1
+        rows = spec["n_sink"] + spec["window"] + (0 if cache == "v2" else 1)
         g = torch.Generator(device=device).manual_seed(seed)
         for layer in self.cache.layers:
             for r0 in range(0, rows, 4096):
@@ -564,6 +632,11 @@ class ModelBench:
         return sum(l._kbuf.numel() * l._kbuf.element_size() + l._vbuf.numel() * l._vbuf.element_size()
                    for l in self.cache.layers)
 
+    def step_kernels(self) -> int:
+        """Sink-cache kernels per decode step: v1 halo + stream + combine, v2 place + attention
+        + combine, per layer (an upper bound when a layer's plan has a single split)."""
+        return 3 * self.cfg.num_hidden_layers
+
 
 def run_model(args, workload: str) -> None:
     from attention_sinks_b200 import streams
@@ -577,7 +650,7 @@ def run_model(args, workload: str) -> None:
     waves = [min(wave, mine - w0) for w0 in range(0, mine, wave)]
     elapsed, launches = 0.0, 0
     for wi, nb in enumerate(waves):
-        bench = ModelBench(spec, nb, device, seed=1000 * rank + wi)
+        bench = ModelBench(spec, nb, device, seed=1000 * rank + wi, cache=args.cache)
         for i in range(args.warmup):  # eager steps (eviction starts), capture, replays
             bench.step(i)
         assert bench.cache.is_steady and bench.runner.graph is not None
@@ -590,7 +663,7 @@ def run_model(args, workload: str) -> None:
         end.record()
         end.synchronize()
         elapsed += start.elapsed_time(end) / 1e3
-        launches += 3 * bench.cfg.num_hidden_layers * args.steps
+        launches += bench.step_kernels() * args.steps
         cache_gb = bench.cache_bytes() / 1e9
         del bench
         torch.cuda.empty_cache()
@@ -600,9 +673,10 @@ def run_model(args, workload: str) -> None:
         line = {"metric": METRIC, "value": round(tok / t_max, 1), "unit": "tok/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_max * 1e3 / args.steps, 4),
                 "higher_is_better": True, "scaling": "strong" if spec["partition"] else "weak",
-                "vs_baseline": None, "dtype": "bf16 model / fp32 K", "data": "synthetic (random-init weights, "
+                "vs_baseline": None, "dtype": "bf16 model / fp32 K" if args.cache == "v1" else "bf16 model / bf16 K",
+                "data": "synthetic (random-init weights, "
                 "uniform tokens, cache filled to the steady state)",
-                "config": {"workload": workload, "streams_total": total, "streams_per_gpu": mine,
+                "config": {"workload": workload, "cache": args.cache, "streams_total": total, "streams_per_gpu": mine,
                            "waves_per_gpu": len(waves), "n_sink": spec["n_sink"], "window": spec["window"],
                            "layers": model_configs()[workload]["cfg"]().num_hidden_layers,
                            "cache_gb_per_wave": round(cache_gb, 2), "runner": "StreamRunner (CUDA graph)"},
@@ -627,8 +701,8 @@ def op_kinds() -> dict:
                             f"GQA decode attention over window + 1 + n_sink rows, Qwen3-0.6B layer shape "
                             f"(Hq {HQ}, Hkv {HKV}, head_dim {D})",
                    key_dtype="bf16", dtype="bf16",
-                   kernel="sink_stream_kernel<bf16, bf16, 128, 2, true> attend-only (timed with the place "
-                          "kernel and split combine: the whole v2 step)",
+                   kernel="sink_attend_tc_kernel<bf16, 2> (tcgen05, persistent; timed with the place kernel "
+                          "and the split combine: the whole v2 step)",
                    api="SinkLayerV2.update + decode_attention_forward (fused step)"),
     }
 
@@ -645,11 +719,13 @@ def main():
                     help="v1: SinkCache fused step (default); v2: SinkCacheV2 ring-buffer step")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="op", choices=["op"] + sorted(model_configs()),
+    ap.add_argument("--workload", default="op", choices=["op", "chunk"] + sorted(model_configs()),
                     help="op: the layer-step (default); otherwise a model-level streamed run")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.workload == "chunk":
+        return chunk_bench(args)
     if args.workload != "op":
         return run_model(args, args.workload)
 

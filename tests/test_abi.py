@@ -68,16 +68,22 @@ def test_workspace_and_plan_are_host_arithmetic(built_lib):
     (_lib.OP_FUSED_STEP, 257, 4, 252, 0),
 ])
 @pytest.mark.parametrize("batch", [1, 8, 64])
-def test_plan_covers_rows_exactly(op, rows, n_sink, window, drop, batch):
+@pytest.mark.parametrize("kdt", [torch.float32, torch.bfloat16], ids=["k32", "k16"])
+def test_plan_covers_rows_exactly(op, rows, n_sink, window, drop, batch, kdt):
     """Splits tile each pair's rows with no gap and no empty split, in items of at most 32
-    chunks (about 4 or more when the step takes several waves)."""
-    p = _lib.plan(op, batch, 8, 16, 128, torch.float32, torch.bfloat16, rows, n_sink, window, drop, 148)
+    chunks (about 4 or more when the step takes several waves).  16-bit K attention plans
+    for the persistent tensor-core kernel: 128-row chunks, one CTA per SM, items of 2 or
+    more chunks."""
+    p = _lib.plan(op, batch, 8, 16, 128, kdt, torch.bfloat16, rows, n_sink, window, drop, 148)
+    if op == _lib.OP_ATTEND and kdt == torch.bfloat16:
+        assert p["chunk_rows"] == 128 and p["stages"] == 3
     total = window if op == _lib.OP_EVICT else rows
     ns, rps, t = p["splits"], p["rows_per_split"], p["chunk_rows"]
     assert rps % t == 0 and 1 <= ns <= 256 and rps <= 32 * t
     assert (ns - 1) * rps < total <= ns * rps
-    if batch * 8 * ns > 296:  # several waves: items of about 4 chunks or more (evened out)
-        assert rps >= min(3 * t, -(-total // t) * t)
+    slots = 148 * (233472 // (p["smem_bytes"] + 1024))  # CTA slots: SMs x CTAs per SM
+    if batch * 8 * ns > slots:  # several waves: items of about 4 (tensor-core kernel: 2) chunks or more
+        assert rps >= min((2 if t == 128 else 3) * t, -(-total // t) * t)
 
 
 def test_argument_errors_return_codes_without_a_gpu(built_lib):
