@@ -23,7 +23,7 @@ _DTYPE_CODE = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float
 EXPORTED_SYMBOLS = (
     "sink_abi_version", "sink_strerror", "sink_workspace_bytes", "sink_plan", "sink_append",
     "sink_evict_rerotate", "sink_decode_attention", "sink_fused_decode_step", "sink_read_status",
-    "sink_decode_attention_noalloc", "sink_v2_place", "sink_v2_decode_step",
+    "sink_decode_attention_noalloc", "sink_v2_place", "sink_v2_decode_step", "sink_prepare_device",
 )
 NOALLOC_SCRATCH_BYTES = 16 << 20
 ESCRATCH = -8
@@ -69,6 +69,7 @@ def _declare(lib):
         "sink_fused_decode_step": (i32, [pkv, prows, prows, prows, i32, i32, i32, i32, fp, fp, i32,
                                          ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
         "sink_read_status": (i32, [vp, vp, pi32]),
+        "sink_prepare_device": (i32, []),
         "sink_decode_attention_noalloc": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, vp, i64, i64, vp]),
         "sink_v2_place": (i32, [pkv, prows, prows, prows, vp, i32, prows, vp, i64, i32, i32, vp, i32, vp]),
         "sink_v2_decode_step": (i32, [pkv, prows, prows, prows, vp, i32, vp, i32, i32, vp, i32, prows,
@@ -129,8 +130,8 @@ def kv_desc(kbuf: torch.Tensor, vbuf: torch.Tensor) -> KVBuffers:
         raise ValueError(f"K/V buffers must be [B, H, slots, D] of one shape, got {tuple(kbuf.shape)}, "
                          f"{tuple(vbuf.shape)}")
     d = kbuf.shape[-1]
-    for t in (kbuf, vbuf):
-        if t.stride(-1) != 1 or t.stride(-2) != d:
+    for t in (kbuf, vbuf):  # a single row has no row stride to check
+        if t.stride(-1) != 1 or (t.shape[-2] > 1 and t.stride(-2) != d):
             raise ValueError("cache buffers need contiguous rows (stride[-2] == head_dim, stride[-1] == 1)")
     b, h, s, _ = kbuf.shape
     return KVBuffers(kbuf.data_ptr(), vbuf.data_ptr(), dtype_code(kbuf.dtype), dtype_code(vbuf.dtype),
@@ -152,6 +153,21 @@ def stream_handle(device: torch.device) -> int:
 
 
 _sm_count = {}
+
+
+_prepared: set[int] = set()
+
+
+def prepare_device(device: torch.device) -> None:
+    """The library's one-time set-up of `device` (kernel shared-memory opt-ins, the tensor-map
+    encoder lookup): must run outside any CUDA-graph capture, so the caches call it at lazy
+    initialisation."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx in _prepared:
+        return
+    with torch.cuda.device(idx):
+        _check(lib().sink_prepare_device(), "sink_prepare_device")
+    _prepared.add(idx)
 
 
 def sm_count(device: torch.device) -> int:

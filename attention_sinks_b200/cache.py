@@ -80,6 +80,7 @@ class SinkLayer(CacheLayerMixin):
     def lazy_initialization(self, key_states, value_states):
         self.dtype, self.device = key_states.dtype, key_states.device
         _lib.check_device(self.device)
+        _lib.prepare_device(self.device)  # before any graph capture of this layer's steps
         self.key_dtype = self.key_dtype or self.dtype
         self.inv_freq = self.inv_freq.to(self.device)
         if self.rerotate_keys and 2 * self.inv_freq.numel() != key_states.shape[-1]:

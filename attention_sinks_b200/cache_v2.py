@@ -60,6 +60,7 @@ class SinkLayerV2(CacheLayerMixin):
     def lazy_initialization(self, key_states, value_states):
         self.dtype, self.device = key_states.dtype, key_states.device
         _lib.check_device(self.device)
+        _lib.prepare_device(self.device)  # before any graph capture of this layer's steps
         b, h, _, d = key_states.shape
         if 2 * self.inv_freq.numel() > d:
             raise ValueError(f"rotary dims {2 * self.inv_freq.numel()} exceed head_dim {d}")
@@ -97,6 +98,18 @@ class SinkLayerV2(CacheLayerMixin):
 
     def _window_start(self, t: int) -> int:
         return max(min(t, self.n_sink), t - self.window)
+
+    def _ring_rows(self, buf: torch.Tensor, lo: int, hi: int) -> list[torch.Tensor]:
+        """Rows of positions [lo, hi) (all >= n_sink, fewer than a ring) in position order, as
+        at most two contiguous views of the ring: the same rows the reference gathers with an
+        index list (cache_v2.py:189-193), without the gather."""
+        n = hi - lo
+        if n <= 0:
+            return []
+        s0 = (lo - self.n_sink) % self.ring
+        if s0 + n <= self.ring:
+            return [buf[:, :, s0:s0 + n]]
+        return [buf[:, :, s0:self.ring], buf[:, :, :s0 + n - self.ring]]
 
     # ------------------------------------------------------------------ rotation
 
@@ -207,15 +220,10 @@ class SinkLayerV2(CacheLayerMixin):
         t, q = self.t, k.shape[-2]
         ws = self._window_start(t)
         R = len(self.region_pos)
-        win = range(max(ws, self.n_sink), t)
-        slots = self._slots(win.start, win.stop)
+        lo = max(ws, self.n_sink)
         r = self.ring
-        b, h, _, d = self._kbuf.shape
-        keys = torch.empty(b, h, R + len(win) + q, d, dtype=self.dtype, device=self.device)
-        self._rotate_region(t, keys[:, :, :R])
-        keys[:, :, R:R + len(win)] = self._kbuf.index_select(2, slots)
-        keys[:, :, R + len(win):] = k
-        values = torch.cat((self._vbuf[:, :, r:r + R], self._vbuf.index_select(2, slots), v), -2)
+        keys = torch.cat((self._rotate_region(t), *self._ring_rows(self._kbuf, lo, t), k), -2)
+        values = torch.cat((self._vbuf[:, :, r:r + R], *self._ring_rows(self._vbuf, lo, t), v), -2)
 
         for i in range(q):
             if t + i < self.n_sink:
@@ -263,10 +271,9 @@ class SinkLayerV2(CacheLayerMixin):
         ws = self._window_start(t)
         R = len(self.region_pos)
         win = list(range(max(ws, self.n_sink), t))
-        slots = self._slots(max(ws, self.n_sink), t)
         r = self.ring
-        k = torch.cat((self._rotate_region(t), self._kbuf.index_select(2, slots)), -2)
-        v = torch.cat((self._vbuf[:, :, r:r + R], self._vbuf.index_select(2, slots)), -2)
+        k = torch.cat((self._rotate_region(t), *self._ring_rows(self._kbuf, win[0] if win else t, t)), -2)
+        v = torch.cat((self._vbuf[:, :, r:r + R], *self._ring_rows(self._vbuf, win[0] if win else t, t)), -2)
         return k, v, [ws - R + j for j in range(R)] + win
 
     def reset(self) -> None:

@@ -171,6 +171,8 @@ int device_sms(int* dev_out) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+int32_t prepare_device(int dev);
+
 int32_t check_kv(const sink_kv_buffers_t* kv) {
   if (!kv || !kv->k || !kv->v) return SINK_EINVAL;
   if (kv->batch < 1 || kv->heads_kv < 1 || kv->slots < 1) return SINK_EINVAL;
@@ -226,13 +228,8 @@ int32_t launch_stream(const StreamArgs& A, const Plan& pl, int pairs, cudaStream
   using Gm = StreamGeom<KT, VT, D>;
   if (Gm::SMEM != pl.smem || Gm::T != pl.T) return SINK_EINVAL;  // host/device geometry drift
   auto kern = sink_stream_kernel<KT, VT, D, GMAX, ATTEND>;
-  static std::atomic<uint64_t> configured{0};
-  const uint64_t bit = uint64_t(1) << dev;
-  if (!(configured.load(std::memory_order_acquire) & bit)) {
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::SMEM);
-    if (err != cudaSuccess) return err;
-    configured.fetch_or(bit, std::memory_order_acq_rel);
-  }
+  const int32_t rc = prepare_device(dev);
+  if (rc) return rc;
   return launch_dependent(kern, dim3(pl.ns, pairs), Gm::SMEM, st, A);
 }
 
@@ -415,13 +412,8 @@ int32_t encode_query_map(CUtensorMap* map, const sink_rows_t* q, int batch, int 
 template <typename T, int GMAX>
 int32_t launch_tc_g(const TcArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev) {
   auto kern = sink_attend_tc_kernel<T, GMAX>;
-  static std::atomic<uint64_t> configured{0};  // per instantiation: one bit per device
-  const uint64_t bit = uint64_t(1) << dev;
-  if (!(configured.load(std::memory_order_acquire) & bit)) {
-    const cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
-    if (err != cudaSuccess) return err;
-    configured.fetch_or(bit, std::memory_order_acq_rel);
-  }
+  const int32_t rc = prepare_device(dev);
+  if (rc) return rc;
   const int sms = device_sms(&dev);
   if (sms <= 0) return SINK_EDEVICE;
   const long items = long(pl.ns) * pairs;
@@ -632,6 +624,74 @@ int32_t launch_v2_place(const sink_kv_buffers_t* kv, const V2PlaceArgs& a, int s
     case SINK_DTYPE_F32: return launch_v2_place_t<float>(kv->head_dim, a, sms, st);
     default: return SINK_EDTYPE;
   }
+}
+
+
+// ---------------------------------------------------------------- per-device set-up
+
+// Opt every kernel that uses more than 48 KB of dynamic shared memory into its size, and
+// look up the tensor-map encoder: calls that must not happen inside a stream capture, so
+// they are made once per device, by sink_prepare_device() or by the first launch.
+template <bool ATTEND, typename KT, typename VT, int D>
+cudaError_t allow_smem_d() {
+  const int bytes = StreamGeom<KT, VT, D>::SMEM;
+  if constexpr (!ATTEND) {
+    return cudaFuncSetAttribute(sink_stream_kernel<KT, VT, D, 1, false>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  } else {
+    cudaError_t e = cudaFuncSetAttribute(sink_stream_kernel<KT, VT, D, 1, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(sink_stream_kernel<KT, VT, D, 2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(sink_stream_kernel<KT, VT, D, 4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(sink_stream_kernel<KT, VT, D, 8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    return e;
+  }
+}
+
+template <bool ATTEND, typename KT, typename VT>
+cudaError_t allow_smem_t() {
+  cudaError_t e = allow_smem_d<ATTEND, KT, VT, 64>();
+  if (e == cudaSuccess) e = allow_smem_d<ATTEND, KT, VT, 128>();
+  if (e == cudaSuccess) e = allow_smem_d<ATTEND, KT, VT, 256>();
+  return e;
+}
+
+template <bool ATTEND>
+cudaError_t allow_smem_stream() {
+  cudaError_t e = allow_smem_t<ATTEND, float, __nv_bfloat16>();
+  if (e == cudaSuccess) e = allow_smem_t<ATTEND, __nv_bfloat16, __nv_bfloat16>();
+  if (e == cudaSuccess) e = allow_smem_t<ATTEND, float, __half>();
+  if (e == cudaSuccess) e = allow_smem_t<ATTEND, __half, __half>();
+  if (e == cudaSuccess) e = allow_smem_t<ATTEND, float, float>();
+  return e;
+}
+
+template <typename T>
+cudaError_t allow_smem_tc() {
+  const int b = kTcSmemBytes;
+  cudaError_t e = cudaFuncSetAttribute(sink_attend_tc_kernel<T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(sink_attend_tc_kernel<T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(sink_attend_tc_kernel<T, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(sink_attend_tc_kernel<T, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+  return e;
+}
+
+std::atomic<uint64_t> g_prepared{0};  // one bit per device
+
+int32_t prepare_device(int dev) {
+  const uint64_t bit = uint64_t(1) << dev;
+  if (g_prepared.load(std::memory_order_acquire) & bit) return SINK_OK;
+  cudaError_t e = allow_smem_stream<false>();
+  if (e == cudaSuccess) e = allow_smem_stream<true>();
+  if (e == cudaSuccess) e = allow_smem_tc<__nv_bfloat16>();
+  if (e == cudaSuccess) e = allow_smem_tc<__half>();
+  if (e != cudaSuccess) return e;
+  if (tensor_map_encoder() == nullptr) return SINK_EDEVICE;
+  g_prepared.fetch_or(bit, std::memory_order_acq_rel);
+  return SINK_OK;
 }
 
 }  // namespace
@@ -857,6 +917,12 @@ int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_ne
   if ((rc = launch_v2_place(kv, a, sms, st))) return rc;
   return launch_attention(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
                           out_stride_h, workspace, pl, dev, st);
+}
+
+int32_t sink_prepare_device(void) {
+  int dev = 0;
+  if (device_sms(&dev) <= 0) return SINK_EDEVICE;
+  return prepare_device(dev);
 }
 
 int32_t sink_read_status(void* workspace, void* stream, int32_t* status) {

@@ -31,6 +31,10 @@ def flash_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float
     if q_len != 1 or hq % k.shape[1]:
         raise ValueError(f"flash_decode needs one query token and Hq % Hkv == 0, got q {tuple(q.shape)}, "
                          f"k {tuple(k.shape)}")
+    if k.shape[-2] > 1 and k.stride(-2) != dim:  # rows must be contiguous for the bulk copies
+        k = k.contiguous()
+    if v.shape[-2] > 1 and v.stride(-2) != dim:
+        v = v.contiguous()
     out = torch.empty(bsz, 1, hq, dim, device=q.device, dtype=q.dtype)
     ws = _lib.Workspace()  # per call, like the reference's partials: safe under graph capture
     return _lib.decode_attention(q, k, v, k.shape[2], scale, out, ws, mask)

@@ -29,6 +29,7 @@ class StreamRunner:
         self.static_ids = self.static_logits = self.static_pos = None
         self._key = None
         self.replays = 0
+        self._warmed = False
 
     @torch.no_grad()
     def step(self, ids: torch.Tensor) -> torch.Tensor:
@@ -68,6 +69,14 @@ class StreamRunner:
                 self.cache.layout_key() if self.v2 else None)
 
     def _capture(self, ids):
+        if not self._warmed:
+            # Libraries the model calls set themselves up on first use (cuBLAS handles,
+            # lazily loaded kernels), which cannot happen inside a capture.  A v2 cache is
+            # steady right after its fill, so the first step may be a capture: run one
+            # forward without the cache first (it leaves the cache untouched).
+            self.model(ids, use_cache=False)
+            torch.cuda.synchronize()
+            self._warmed = True
         self._key = self._layout()
         self.static_ids = ids.clone()
         kwargs = {}

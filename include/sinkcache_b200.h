@@ -182,6 +182,15 @@ int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k
 int32_t sink_read_status(void* workspace, void* stream, int32_t* status);
 
 /*
+ * One-time set-up of the current device: opts the kernels into their shared-memory sizes
+ * and looks up the driver's tensor-map encoder.  These calls cannot be made inside a CUDA
+ * stream capture, so call this once per device before capturing any launch of this
+ * library into a graph (every entry point also runs it on its first use).  No counterpart
+ * in the reference (its Triton kernels compile on first use instead).
+ */
+int32_t sink_prepare_device(void);
+
+/*
  * Ring-buffer cache (SinkLayerV2, src/sinkcache/cache_v2.py:59-248).  Window keys stay at the
  * rotation the model gave them (absolute positions); only the region -- the sinks and any
  * pinned tokens -- is re-rotated, from stored originals, to sit just before the window.

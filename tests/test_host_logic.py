@@ -58,6 +58,7 @@ def cpu_kernels(monkeypatch):
         return wrapped
 
     monkeypatch.setattr(_lib, "check_device", lambda device: None)
+    monkeypatch.setattr(_lib, "prepare_device", lambda device: None)
     monkeypatch.setattr(_lib, "sm_count", lambda device: 148)
     monkeypatch.setattr(_lib, "evict_rerotate", count("evict", fake_evict))
     monkeypatch.setattr(_lib, "append", count("append", fake_append))

@@ -53,6 +53,7 @@ def cpu_v2(monkeypatch):
         return wrapped
 
     monkeypatch.setattr(_lib, "check_device", lambda device: None)
+    monkeypatch.setattr(_lib, "prepare_device", lambda device: None)
     monkeypatch.setattr(_lib, "sm_count", lambda device: 148)
     monkeypatch.setattr(_lib, "v2_place", count("place", fake_place))
     monkeypatch.setattr(_lib, "v2_decode_step", count("fused", fake_decode_step))
