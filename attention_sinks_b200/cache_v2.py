@@ -99,6 +99,22 @@ class SinkLayerV2(CacheLayerMixin):
     def _window_start(self, t: int) -> int:
         return max(min(t, self.n_sink), t - self.window)
 
+    def _assemble(self, R: int, window: list[torch.Tensor], chunk: torch.Tensor | None,
+                  region: torch.Tensor | None = None) -> torch.Tensor:
+        """[region (R rows), window rows, chunk] in one new tensor, filled by slice copies
+        (torch.cat of these strided views runs far below the copy bandwidth).  Region rows
+        are copied from `region`, or left for the caller to write when it is None."""
+        b, h, _, d = self._kbuf.shape
+        n = R + sum(x.shape[-2] for x in window) + (chunk.shape[-2] if chunk is not None else 0)
+        out = torch.empty(b, h, n, d, dtype=self.dtype, device=self.device)
+        if region is not None and R:
+            out[:, :, :R].copy_(region)
+        o = R
+        for x in window + ([chunk] if chunk is not None else []):
+            out[:, :, o:o + x.shape[-2]].copy_(x)
+            o += x.shape[-2]
+        return out
+
     def _ring_rows(self, buf: torch.Tensor, lo: int, hi: int) -> list[torch.Tensor]:
         """Rows of positions [lo, hi) (all >= n_sink, fewer than a ring) in position order, as
         at most two contiguous views of the ring: the same rows the reference gathers with an
@@ -222,8 +238,9 @@ class SinkLayerV2(CacheLayerMixin):
         R = len(self.region_pos)
         lo = max(ws, self.n_sink)
         r = self.ring
-        keys = torch.cat((self._rotate_region(t), *self._ring_rows(self._kbuf, lo, t), k), -2)
-        values = torch.cat((self._vbuf[:, :, r:r + R], *self._ring_rows(self._vbuf, lo, t), v), -2)
+        keys = self._assemble(R, self._ring_rows(self._kbuf, lo, t), k)
+        self._rotate_region(t, keys[:, :, :R])
+        values = self._assemble(R, self._ring_rows(self._vbuf, lo, t), v, self._vbuf[:, :, r:r + R])
 
         for i in range(q):
             if t + i < self.n_sink:
@@ -272,8 +289,10 @@ class SinkLayerV2(CacheLayerMixin):
         R = len(self.region_pos)
         win = list(range(max(ws, self.n_sink), t))
         r = self.ring
-        k = torch.cat((self._rotate_region(t), *self._ring_rows(self._kbuf, win[0] if win else t, t)), -2)
-        v = torch.cat((self._vbuf[:, :, r:r + R], *self._ring_rows(self._vbuf, win[0] if win else t, t)), -2)
+        lo = win[0] if win else t
+        k = self._assemble(R, self._ring_rows(self._kbuf, lo, t), None)
+        self._rotate_region(t, k[:, :, :R])
+        v = self._assemble(R, self._ring_rows(self._vbuf, lo, t), None, self._vbuf[:, :, r:r + R])
         return k, v, [ws - R + j for j in range(R)] + win
 
     def reset(self) -> None:
