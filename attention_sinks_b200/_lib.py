@@ -62,7 +62,7 @@ def _declare(lib):
         "sink_abi_version": (i32, []),
         "sink_strerror": (ctypes.c_char_p, [i32]),
         "sink_workspace_bytes": (sz, [i32] * 12),
-        "sink_plan": (i32, [i32] * 12 + [pi32] * 5),
+        "sink_plan": (i32, [i32] * 12 + [pi32] * 6),
         "sink_append": (i32, [pkv, prows, prows, i32, vp]),
         "sink_evict_rerotate": (i32, [pkv, i32, i32, i32, fp, fp, i32, vp, sz, vp]),
         "sink_decode_attention": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
@@ -191,11 +191,11 @@ def workspace_bytes(op: int, batch: int, heads_kv: int, heads_q: int, head_dim: 
 
 def plan(op: int, batch: int, heads_kv: int, heads_q: int, head_dim: int, k_dtype: torch.dtype,
          v_dtype: torch.dtype, rows: int, n_sink: int, window: int, drop: int, num_sms: int) -> dict:
-    out = [ctypes.c_int32() for _ in range(5)]
+    out = [ctypes.c_int32() for _ in range(6)]
     rc = lib().sink_plan(op, batch, heads_kv, heads_q, head_dim, dtype_code(k_dtype), dtype_code(v_dtype),
                          rows, n_sink, window, drop, num_sms, *[ctypes.byref(o) for o in out])
     _check(rc, "sink_plan")
-    keys = ("splits", "rows_per_split", "chunk_rows", "stages", "smem_bytes")
+    keys = ("splits", "rows_per_split", "chunk_rows", "stages", "smem_bytes", "cluster_ctas")
     return {k: o.value for k, o in zip(keys, out)}
 
 

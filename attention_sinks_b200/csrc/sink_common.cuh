@@ -18,6 +18,11 @@ constexpr int kSmemPerSM = 233472;            // B200: 228 KB shared memory per 
 constexpr int kSmemReservedPerCTA = 1024;
 constexpr int kMaxSplits = 256;               // combine kernel keeps ns * G weights in smem
 constexpr int kMaxGroup = 8;
+// Clustered launches (every split of a pair in one thread-block cluster): at most this many
+// splits (a non-portable cluster size), and a shift of at most kClusterHaloRows rows, whose
+// halo rows each CTA stages in its own shared memory.
+constexpr int kClusterMax = 16;
+constexpr int kClusterHaloRows = 4;
 
 __host__ __device__ inline int imin(int a, int b) { return a < b ? a : b; }
 __host__ __device__ inline int imax(int a, int b) { return a > b ? a : b; }
@@ -55,6 +60,11 @@ struct StreamArgs {
   char* halo_k;
   char* halo_v;
   int* status;
+  // 1: launched as clusters of ns CTAs along x (one cluster per pair).  Halo rows are then
+  // staged in shared memory before a cluster barrier, and the split partials are merged
+  // through distributed shared memory: no halo pre-pass, no combine kernel, no workspace
+  // beyond the status word.
+  int cluster;
 };
 
 // Rows [a, e) of split j.
@@ -170,6 +180,23 @@ __device__ __forceinline__ void grid_dependency_wait() {
 }
 __device__ __forceinline__ void allow_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Thread-block cluster: a hardware barrier over every thread of the cluster (release /
+// acquire orders shared and global memory across its CTAs), and reads of another CTA's
+// shared memory through the cluster window.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
 }
 
 // ------------------------------------------------------------------ element conversions
@@ -295,9 +322,12 @@ struct StreamGeom {
   static constexpr int STAGE = T * (KROW + VROW);
   static constexpr int S0 = kPipeBytes / STAGE;
   static constexpr int S = S0 < 2 ? 2 : (S0 > 4 ? 4 : S0);
-  static constexpr int SMEM = kBarrierBytes + S * STAGE;
-  // the end-of-split merge reuses the stage memory
-  static_assert(kWarps * kMaxGroup * (D + 2) * 4 <= S * STAGE, "merge scratch");
+  static constexpr int HALO = kClusterHaloRows * (KROW + VROW);  // clustered launches' halo rows
+  static constexpr int SMEM = kBarrierBytes + S * STAGE + HALO;
+  // the end-of-split merge reuses the stage memory: per-warp partials, then (clustered) the
+  // CTA's merged partial that the other CTAs of its cluster read
+  static_assert((kWarps + 1) * kMaxGroup * (D + 2) * 4 <= S * STAGE, "merge scratch");
+  static_assert(kBarrierBytes >= 8 * (S + 1), "stage barriers and the halo barrier");
 };
 
 }  // namespace sinkb200

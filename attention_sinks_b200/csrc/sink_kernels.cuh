@@ -113,6 +113,10 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
   extern __shared__ __align__(128) unsigned char smem[];
   const uint32_t bar0 = smem_addr(smem);
   unsigned char* stages = smem + kBarrierBytes;
+  unsigned char* halo_sk = stages + S * STAGE;  // clustered: this split's halo rows
+  unsigned char* halo_sv = halo_sk + kClusterHaloRows * KROW;
+  const uint32_t halo_bar = bar0 + 8 * S;
+  const bool clustered = A.cluster != 0;  // grid-uniform
 
   grid_dependency_wait();  // halo copies (or the producers of q, k, v) complete
   const int tid = threadIdx.x;
@@ -123,22 +127,27 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
   split_rows(A.row_begin, A.row_end, A.rows_per_split, j, a, e);
   int hlo, hhi;
   halo_range(A.n_sink, A.window, A.drop, A.written_end, j >= A.ns - 1, a, e, hlo, hhi);
+  const bool has_halo = hlo < hhi;
 
   KT* kb = reinterpret_cast<KT*>(A.kbuf) + b * A.k_sb + h * A.k_sh;
   VT* vb = reinterpret_cast<VT*>(A.vbuf) + b * A.v_sb + h * A.v_sh;
   const size_t halo_row0 = (size_t(p) * A.ns + j) * A.halo_rows;
-  const unsigned char* hk = reinterpret_cast<const unsigned char*>(A.halo_k) + halo_row0 * KROW;
-  const unsigned char* hv = reinterpret_cast<const unsigned char*>(A.halo_v) + halo_row0 * VROW;
+  // Unclustered: halo rows come from the workspace copy made by sink_halo_kernel.
+  // Clustered: issue_rows leaves them out and the consumer copies them from halo_sk/halo_sv.
+  const unsigned char* hk =
+      clustered ? nullptr : reinterpret_cast<const unsigned char*>(A.halo_k) + halo_row0 * KROW;
+  const unsigned char* hv =
+      clustered ? nullptr : reinterpret_cast<const unsigned char*>(A.halo_v) + halo_row0 * VROW;
   const int nchunks = (e - a + T - 1) / T;
 
   if (tid == 0) {
 #pragma unroll
     for (int s = 0; s < S; ++s) mbar_init(bar0 + 8 * s, 1);
+    mbar_init(halo_bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
 
-  // Halo rows come from the workspace copy made by sink_halo_kernel.
   auto issue_chunk = [&](int c) {
     const int x = a + c * T, xe = imin(x + T, e);
     const uint32_t sk = smem_addr(stages + (c % S) * STAGE);
@@ -146,8 +155,23 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
   };
 
   if (tid == 0) {
+    if (clustered && has_halo) {  // hhi - hlo <= drop <= kClusterHaloRows rows (host-checked)
+      const uint32_t n = uint32_t(hhi - hlo);
+      mbar_arrive_expect_tx(halo_bar, n * (KROW + VROW));
+      bulk_g2s(smem_addr(halo_sk), kb + size_t(hlo) * D, n * KROW, halo_bar);
+      bulk_g2s(smem_addr(halo_sv), vb + size_t(hlo) * D, n * VROW, halo_bar);
+    }
     const int pro = imin(S - 1, nchunks);
     for (int c = 0; c < pro; ++c) issue_chunk(c);
+  }
+
+  bool failed = false;
+  if (clustered) {
+    // Every CTA of the cluster holds its halo rows before any CTA stores: a split reads the
+    // first rows of the next split before that split overwrites them.  Only loads precede
+    // this barrier.
+    if (has_halo && !mbar_wait_bounded(halo_bar, 0)) failed = true;
+    cluster_sync();
   }
 
   Lanes L;
@@ -155,7 +179,6 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
   L.begin_pair(A, b, h);
   const uint8_t* mrow = A.mask != nullptr ? A.mask + b * A.mask_sb : nullptr;
 
-  bool failed = false;
 #pragma unroll 1
   for (int c = 0; c < nchunks; ++c) {
     const int stage = c % S;
@@ -166,6 +189,16 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
     if (A.append_row >= x && A.append_row < xe) {  // CTA-uniform
       fill_append_row<KT, VT, D>(A, b, h, sk, sv, A.append_row - x);
       __syncthreads();
+    }
+    if (clustered && has_halo) {  // output rows whose sources are the staged halo rows
+      const int r0 = imax(x, hlo - A.drop), r1 = imin(xe, hhi - A.drop);
+      if (r0 < r1) {  // CTA-uniform
+        copy_rows<KROW, VROW>(reinterpret_cast<unsigned char*>(sk) + (r0 - x) * KROW,
+                              reinterpret_cast<unsigned char*>(sv) + (r0 - x) * VROW,
+                              halo_sk + (r0 + A.drop - hlo) * KROW, halo_sv + (r0 + A.drop - hlo) * VROW,
+                              r1 - r0);
+        __syncthreads();
+      }
     }
     if (!failed) L.chunk(sk, sv, x, xe, A, mrow);
     int st_lo, st_hi;
@@ -186,34 +219,70 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
     }
   }
   if (tid == 0) bulk_wait<0>();
-  __syncthreads();
+  failed = __syncthreads_or(failed);
   allow_dependents();
-  if (failed) {
-    if (tid == 0) atomicOr(A.status, 1);
-    return;
-  }
+  if (failed && tid == 0) atomicOr(A.status, 1);
+  // A clustered CTA stays for the cluster barriers below (its results are void).
+  if (failed && !clustered) return;
 
   if constexpr (ATTEND) {
     float* scratch = reinterpret_cast<float*>(stages);
     L.to_scratch(scratch);
     __syncthreads();
     const int G = A.group;
+    if (!clustered) {
+      for (int idx = tid; idx < G * D; idx += kThreads) {
+        const int g = idx / D, d = idx - g * D;
+        float M, Ls, O;
+        Lanes::from_scratch(scratch, g, d, M, Ls, O);
+        if (A.ns == 1) {
+          VT* o = reinterpret_cast<VT*>(A.out) + b * A.o_sb + (h * G + g) * A.o_sh;
+          o[d] = Elem<VT>::from_f(O / Ls);
+        } else {
+          const size_t part = (size_t(p) * A.ns + j) * G + g;
+          A.o_part[part * D + d] = O;
+          if (d == 0) {
+            A.m_part[part] = M;
+            A.l_part[part] = Ls;
+          }
+        }
+      }
+      return;
+    }
+    // Clustered: this CTA's partial (O[g][d], then M[g], L[g]) stays in shared memory; after
+    // the barrier every CTA merges a slice of the pair's G * D outputs from all ns partials.
+    float* part = scratch + kWarps * GMAX * (D + 2);
     for (int idx = tid; idx < G * D; idx += kThreads) {
       const int g = idx / D, d = idx - g * D;
       float M, Ls, O;
       Lanes::from_scratch(scratch, g, d, M, Ls, O);
-      if (A.ns == 1) {
-        VT* o = reinterpret_cast<VT*>(A.out) + b * A.o_sb + (h * G + g) * A.o_sh;
-        o[d] = Elem<VT>::from_f(O / Ls);
-      } else {
-        const size_t part = (size_t(p) * A.ns + j) * G + g;
-        A.o_part[part * D + d] = O;
-        if (d == 0) {
-          A.m_part[part] = M;
-          A.l_part[part] = Ls;
-        }
+      part[idx] = O;
+      if (d == 0) {
+        part[G * D + g] = M;
+        part[G * D + G + g] = Ls;
       }
     }
+    cluster_sync();
+    if (!failed) {
+      const uint32_t part_addr = smem_addr(part);
+      for (int idx = j * kThreads + tid; idx < G * D; idx += A.ns * kThreads) {
+        const int g = idx / D, d = idx - g * D;
+        float mx = kNegInf;
+        for (int r = 0; r < A.ns; ++r)
+          mx = fmaxf(mx, ld_cluster_f32(cluster_map(part_addr + 4u * uint32_t(G * D + g), uint32_t(r))));
+        const float mref = mx == kNegInf ? 0.f : mx;
+        float sum = 0.f, o = 0.f;
+        for (int r = 0; r < A.ns; ++r) {
+          const uint32_t base = cluster_map(part_addr, uint32_t(r));
+          const float w = exp2f(ld_cluster_f32(base + 4u * uint32_t(G * D + g)) - mref);
+          sum = __fmaf_rn(w, ld_cluster_f32(base + 4u * uint32_t(G * D + G + g)), sum);
+          o = __fmaf_rn(w, ld_cluster_f32(base + 4u * uint32_t(idx)), o);
+        }
+        VT* op = reinterpret_cast<VT*>(A.out) + b * A.o_sb + (h * G + g) * A.o_sh;
+        op[d] = Elem<VT>::from_f(o / sum);
+      }
+    }
+    cluster_sync();  // no CTA leaves while another still reads its partial
   }
 }
 
@@ -239,20 +308,25 @@ __global__ void __launch_bounds__(kThreads) sink_halo_kernel(const __grid_consta
   const uint4* vbase = reinterpret_cast<const uint4*>(A.vbuf + b * H.v_sb + h * H.v_sh);
   const int j0 = blockIdx.x * kHaloSplitsPerCta;
   const int j1 = imin(j0 + kHaloSplitsPerCta, A.ns - 1);
-  for (int j = j0; j < j1; ++j) {
+  // One flat index space over (split, halo row, 16-byte word), K words then V words, so that
+  // every load of the CTA is independent (a latency-bound copy of a few rows per split).
+  const int kper = A.halo_rows * kv4, vper = A.halo_rows * vv4;
+  const int nk = (j1 - j0) * kper, total = nk + (j1 - j0) * vper;
+  for (int i = threadIdx.x; i < total; i += kThreads) {
+    const bool isk = i < nk;
+    const int per = isk ? kper : vper, w4 = isk ? kv4 : vv4;
+    const int li = isk ? i : i - nk;
+    const int j = j0 + li / per, r = (li % per) / w4, c = li % w4;
     int a, e;
     split_rows(A.row_begin, A.row_end, A.rows_per_split, j, a, e);
     int hlo, hhi;
     halo_range(A.n_sink, A.window, A.drop, A.written_end, false, a, e, hlo, hhi);
-    if (hlo >= hhi) continue;
-    const size_t halo_row0 = (size_t(p) * A.ns + j) * A.halo_rows;
-    const uint4* ks = kbase + size_t(hlo) * kv4;
-    const uint4* vs = vbase + size_t(hlo) * vv4;
-    uint4* kd = reinterpret_cast<uint4*>(A.halo_k) + halo_row0 * kv4;
-    uint4* vd = reinterpret_cast<uint4*>(A.halo_v) + halo_row0 * vv4;
-    const int nk = (hhi - hlo) * kv4, nv = (hhi - hlo) * vv4;
-    for (int i = threadIdx.x; i < nk; i += kThreads) kd[i] = ks[i];
-    for (int i = threadIdx.x; i < nv; i += kThreads) vd[i] = vs[i];
+    if (hlo + r >= hhi) continue;
+    const size_t dst = ((size_t(p) * A.ns + j) * A.halo_rows + r) * w4 + c;
+    if (isk)
+      reinterpret_cast<uint4*>(A.halo_k)[dst] = kbase[size_t(hlo + r) * kv4 + c];
+    else
+      reinterpret_cast<uint4*>(A.halo_v)[dst] = vbase[size_t(hlo + r) * vv4 + c];
   }
 }
 

@@ -35,7 +35,8 @@ bool supported_types(int32_t kdt, int32_t vdt) {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Plan {
-  bool tc = false;  // attention on the tensor-core kernel (sink_attend_tc_kernel)
+  bool tc = false;       // attention on the tensor-core kernel (sink_attend_tc_kernel)
+  bool cluster = false;  // stream kernel launched as one cluster of ns CTAs per pair
   int T = 0, S = 0, stage = 0, smem = 0, ctas_per_sm = 0;
   int ns = 1, rows_per_split = 0, halo_rows = 0;
   size_t off_o = 0, off_m = 0, off_l = 0, off_hk = 0, off_hv = 0, total = 256;
@@ -49,7 +50,7 @@ bool geometry(int D, int ks, int vs, Plan& pl) {
   pl.stage = pl.T * D * (ks + vs);
   int s = kPipeBytes / pl.stage;
   pl.S = s < 2 ? 2 : (s > 4 ? 4 : s);
-  pl.smem = kBarrierBytes + pl.S * pl.stage;
+  pl.smem = kBarrierBytes + pl.S * pl.stage + kClusterHaloRows * D * (ks + vs);
   pl.ctas_per_sm = kSmemPerSM / (pl.smem + kSmemReservedPerCTA);
   if (pl.ctas_per_sm < 1) pl.ctas_per_sm = 1;
   return true;
@@ -104,6 +105,31 @@ void choose_splits(int pairs, int rows, int T, int slots, long target_waves, lon
   pl.rows_per_split = int(tps) * T;
 }
 
+// Clustered stream-kernel launch: every split of a pair in one thread-block cluster, so the
+// step is a single launch (halo rows staged in shared memory behind a cluster barrier, split
+// partials merged through distributed shared memory).  Only for a step whose CTAs fit one
+// wave: there it is bound by launch and memory latency, which the two extra launches of a
+// split step add to; over several waves, clusters that must start together leave CTA slots
+// idle (measured: 256 slots x 64 streams, 57 -> 79 us).  A one-wave plan with more than
+// kClusterMax splits is cut down to kClusterMax when that adds at most kClusterExtraChunks
+// chunks per split (a CTA alone on its SM takes about 2 us per chunk).  A shift of more than
+// kClusterHaloRows rows keeps the halo pre-pass.
+constexpr long kClusterExtraChunks = 4;
+
+void choose_cluster(int pairs, int rows, int T, int slots, int drop, Plan& pl) {
+  if (drop > kClusterHaloRows || pl.ns < 2) return;
+  const long tiles = (rows + T - 1) / T;
+  if (long(pairs) * pl.ns > slots) return;
+  if (pl.ns > kClusterMax) {
+    const long tps0 = pl.rows_per_split / T;
+    const long tps = (tiles + kClusterMax - 1) / kClusterMax;
+    if (tps > kMaxItemChunks || tps - tps0 > kClusterExtraChunks) return;
+    pl.ns = int((tiles + tps - 1) / tps);
+    pl.rows_per_split = int(tps) * T;
+  }
+  pl.cluster = pl.ns > 1;
+}
+
 int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, int32_t D,
                   int32_t kdt, int32_t vdt, int32_t rows, int32_t n_sink, int32_t window,
                   int32_t drop, int32_t num_sms, Plan& pl) {
@@ -131,10 +157,12 @@ int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
   const int pairs = batch * heads_kv;
   if (pl.tc)
     choose_splits(pairs, nrows, pl.T, num_sms, kTcTargetItemsPerCta, kTcMinItemChunks, pl);
-  else
+  else {
     choose_splits(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, kTargetWaves, kMinItemChunks, pl);
+    choose_cluster(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, drop, pl);
+  }
   size_t off = 256;  // status word
-  if (attend && pl.ns > 1) {
+  if (attend && pl.ns > 1 && !pl.cluster) {
     const size_t parts = size_t(pairs) * pl.ns * G;
     pl.off_o = off;
     off += align256(parts * D * 4);
@@ -144,7 +172,7 @@ int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
     off += align256(parts * 4);
   }
   const bool evicts = op == SINK_OP_EVICT || op == SINK_OP_FUSED_STEP;
-  if (evicts && drop > 0 && pl.ns > 1) {
+  if (evicts && drop > 0 && pl.ns > 1 && !pl.cluster) {
     pl.halo_rows = drop < pl.rows_per_split ? drop : pl.rows_per_split;
     const size_t hrows = size_t(pairs) * pl.ns * pl.halo_rows;
     pl.off_hk = off;
@@ -200,22 +228,37 @@ int32_t check_rows(const sink_rows_t* r, int32_t dtype, int32_t batch, int32_t h
 // Launch with programmatic stream serialization: the kernel may begin launching while its
 // predecessor in the stream finishes (every kernel here waits on the grid dependency before
 // touching memory), which hides the launch gap between the halo, stream and combine kernels.
+// With cluster_x > 1 the grid is launched as clusters of cluster_x CTAs along x.
 template <typename... Params, typename... Args>
-int32_t launch_dependent_n(void (*kern)(Params...), dim3 grid, int threads, int smem, cudaStream_t st,
-                           Args... args) {
+int32_t launch_dependent_c(void (*kern)(Params...), dim3 grid, int threads, int smem, int cluster_x,
+                           cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = size_t(smem);
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster_x > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = unsigned(cluster_x);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    n = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = n;
   const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, args...);
   if (err != cudaSuccess) return err;
   return cudaGetLastError();
+}
+
+template <typename... Params, typename... Args>
+int32_t launch_dependent_n(void (*kern)(Params...), dim3 grid, int threads, int smem, cudaStream_t st,
+                           Args... args) {
+  return launch_dependent_c(kern, grid, threads, smem, 1, st, args...);
 }
 
 template <typename... Params, typename... Args>
@@ -230,7 +273,8 @@ int32_t launch_stream(const StreamArgs& A, const Plan& pl, int pairs, cudaStream
   auto kern = sink_stream_kernel<KT, VT, D, GMAX, ATTEND>;
   const int32_t rc = prepare_device(dev);
   if (rc) return rc;
-  return launch_dependent(kern, dim3(pl.ns, pairs), Gm::SMEM, st, A);
+  if (pl.cluster && (pl.ns > kClusterMax || A.cluster != 1)) return SINK_EINVAL;
+  return launch_dependent_c(kern, dim3(pl.ns, pairs), kThreads, Gm::SMEM, pl.cluster ? pl.ns : 1, st, A);
 }
 
 template <bool ATTEND, typename KT, typename VT, int D>
@@ -299,7 +343,7 @@ int32_t launch_combine(int vdt, int D, const StreamArgs& A, int pairs, cudaStrea
 
 int32_t launch_halo(const sink_kv_buffers_t* kv, const StreamArgs& A, const Plan& pl, int pairs,
                     cudaStream_t st) {
-  if (pl.ns < 2 || A.drop <= 0) return SINK_OK;
+  if (pl.ns < 2 || A.drop <= 0 || pl.cluster) return SINK_OK;
   HaloBytes H;
   const int ks = elem_size(kv->k_dtype), vs = elem_size(kv->v_dtype);
   H.k_sb = kv->k_stride_b * ks;
@@ -333,6 +377,7 @@ void fill_common(StreamArgs& A, const sink_kv_buffers_t* kv, const Plan& pl, cha
   A.l_part = pl.off_l ? reinterpret_cast<float*>(ws + pl.off_l) : nullptr;
   A.halo_k = pl.off_hk ? ws + pl.off_hk : nullptr;
   A.halo_v = pl.off_hv ? ws + pl.off_hv : nullptr;
+  A.cluster = pl.cluster ? 1 : 0;
 }
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -509,7 +554,7 @@ int32_t launch_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int3
   const int pairs = kv->batch * kv->heads_kv;
   if ((rc = dispatch_stream<true>(kv->k_dtype, kv->v_dtype, kv->head_dim, A.group, A, pl, pairs, st, dev)))
     return rc;
-  if (pl.ns > 1) return launch_combine(kv->v_dtype, kv->head_dim, A, pairs, st);
+  if (pl.ns > 1 && !pl.cluster) return launch_combine(kv->v_dtype, kv->head_dim, A, pairs, st);
   return SINK_OK;
 }
 
@@ -632,21 +677,26 @@ int32_t launch_v2_place(const sink_kv_buffers_t* kv, const V2PlaceArgs& a, int s
 // Opt every kernel that uses more than 48 KB of dynamic shared memory into its size, and
 // look up the tensor-map encoder: calls that must not happen inside a stream capture, so
 // they are made once per device, by sink_prepare_device() or by the first launch.
+// A stream kernel's dynamic shared memory, and clusters of up to 16 CTAs (above the portable
+// 8; B200 schedules 16 of these 2-per-SM CTAs on one GPC).
+template <typename... Params>
+cudaError_t stream_attrs(void (*kern)(Params...), int bytes) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && kClusterMax > 8)
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
+}
+
 template <bool ATTEND, typename KT, typename VT, int D>
 cudaError_t allow_smem_d() {
   const int bytes = StreamGeom<KT, VT, D>::SMEM;
   if constexpr (!ATTEND) {
-    return cudaFuncSetAttribute(sink_stream_kernel<KT, VT, D, 1, false>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    return stream_attrs(sink_stream_kernel<KT, VT, D, 1, false>, bytes);
   } else {
-    cudaError_t e = cudaFuncSetAttribute(sink_stream_kernel<KT, VT, D, 1, true>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(sink_stream_kernel<KT, VT, D, 2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(sink_stream_kernel<KT, VT, D, 4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(sink_stream_kernel<KT, VT, D, 8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaError_t e = stream_attrs(sink_stream_kernel<KT, VT, D, 1, true>, bytes);
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 2, true>, bytes);
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 4, true>, bytes);
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 8, true>, bytes);
     return e;
   }
 }
@@ -730,7 +780,8 @@ size_t sink_workspace_bytes(int32_t op, int32_t batch, int32_t heads_kv, int32_t
 int32_t sink_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, int32_t head_dim,
                   int32_t k_dtype, int32_t v_dtype, int32_t rows, int32_t n_sink, int32_t window,
                   int32_t drop, int32_t num_sms, int32_t* splits, int32_t* rows_per_split,
-                  int32_t* chunk_rows, int32_t* stages, int32_t* smem_bytes) {
+                  int32_t* chunk_rows, int32_t* stages, int32_t* smem_bytes,
+                  int32_t* cluster_ctas) {
   Plan pl;
   const int32_t rc = make_plan(op, batch, heads_kv, heads_q, head_dim, k_dtype, v_dtype, rows,
                                n_sink, window, drop, num_sms, pl);
@@ -740,6 +791,7 @@ int32_t sink_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
   if (chunk_rows) *chunk_rows = pl.T;
   if (stages) *stages = pl.S;
   if (smem_bytes) *smem_bytes = pl.smem;
+  if (cluster_ctas) *cluster_ctas = pl.cluster ? pl.ns : 1;
   return SINK_OK;
 }
 
@@ -874,7 +926,7 @@ int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k
   if ((rc = launch_halo(kv, A, pl, pairs, st))) return rc;
   if ((rc = dispatch_stream<true>(kv->k_dtype, kv->v_dtype, kv->head_dim, A.group, A, pl, pairs, st, dev)))
     return rc;
-  if (pl.ns > 1) return launch_combine(kv->v_dtype, kv->head_dim, A, pairs, st);
+  if (pl.ns > 1 && !pl.cluster) return launch_combine(kv->v_dtype, kv->head_dim, A, pairs, st);
   return SINK_OK;
 }
 

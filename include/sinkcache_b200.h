@@ -106,13 +106,16 @@ size_t sink_workspace_bytes(int32_t op, int32_t batch, int32_t heads_kv, int32_t
 
 /*
  * Split plan the launch will use (for tests and profiling): number of splits per
- * (batch, head) pair, rows per split, rows per pipeline chunk, pipeline stages and
- * dynamic shared memory per CTA.  Pure host arithmetic.  Returns 0 or SINK_E*.
+ * (batch, head) pair, rows per split, rows per pipeline chunk, pipeline stages, dynamic
+ * shared memory per CTA, and CTAs per thread-block cluster (`splits` when every split of a
+ * pair runs in one cluster and the step is a single launch, else 1).  Pure host
+ * arithmetic.  Returns 0 or SINK_E*.
  */
 int32_t sink_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, int32_t head_dim,
                   int32_t k_dtype, int32_t v_dtype, int32_t rows, int32_t n_sink, int32_t window,
                   int32_t drop, int32_t num_sms, int32_t* splits, int32_t* rows_per_split,
-                  int32_t* chunk_rows, int32_t* stages, int32_t* smem_bytes);
+                  int32_t* chunk_rows, int32_t* stages, int32_t* smem_bytes,
+                  int32_t* cluster_ctas);
 
 /*
  * Append: kv[:, :, row:row+n] = (k_new, v_new)  (k converted to k_dtype exactly, or rounded

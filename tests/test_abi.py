@@ -86,6 +86,29 @@ def test_plan_covers_rows_exactly(op, rows, n_sink, window, drop, batch, kdt):
         assert rps >= min((2 if t == 128 else 3) * t, -(-total // t) * t)
 
 
+@pytest.mark.parametrize("batch,slots,ns,clustered", [
+    (1, 256, 9, True), (1, 1024, 11, True), (2, 4096, 15, True), (4, 4096, 9, True), (8, 1024, 4, True),
+    (1, 4096, 33, False), (64, 256, 3, False), (1, 32768, 37, False), (8, 4096, 33, False),
+    (64, 32768, 33, False),
+])
+def test_plan_clusters_small_steps(batch, slots, ns, clustered, built_lib):
+    """Fused steps whose CTAs fit one wave with at most 16 splits per pair (or 16 splits
+    that add at most 4 chunks per split) run as one clustered launch: no halo or partials
+    workspace.  Several waves, or longer splits, keep the split launch with its halo
+    pre-pass and combine."""
+    f32, bf16 = torch.float32, torch.bfloat16
+    args = (_lib.OP_FUSED_STEP, batch, 8, 16, 128, f32, bf16, slots + 1, 4, slots - 4, 1, 148)
+    p = _lib.plan(*args)
+    assert p["splits"] == ns and (p["cluster_ctas"] == ns) == clustered
+    if not clustered:
+        assert p["cluster_ctas"] == 1
+    ws = _lib.workspace_bytes(*args)
+    assert (ws == 256) == clustered  # the status word alone
+    # a shift of more than 4 rows, or 16-bit K attention on the tensor cores, is never clustered
+    assert _lib.plan(_lib.OP_EVICT, batch, 8, 8, 128, f32, bf16, 0, 4, slots - 4, 5, 148)["cluster_ctas"] == 1
+    assert _lib.plan(_lib.OP_ATTEND, batch, 8, 16, 128, bf16, bf16, slots, 0, 1, 0, 148)["cluster_ctas"] == 1
+
+
 def test_argument_errors_return_codes_without_a_gpu(built_lib):
     """Rejected arguments come back as codes; nothing is launched."""
     kv = _lib.KVBuffers()  # null pointers
