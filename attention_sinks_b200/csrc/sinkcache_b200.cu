@@ -274,7 +274,9 @@ int32_t launch_stream(const StreamArgs& A, const Plan& pl, int pairs, cudaStream
   const int32_t rc = prepare_device(dev);
   if (rc) return rc;
   if (pl.cluster && (pl.ns > kClusterMax || A.cluster != 1)) return SINK_EINVAL;
-  return launch_dependent_c(kern, dim3(pl.ns, pairs), kThreads, Gm::SMEM, pl.cluster ? pl.ns : 1, st, A);
+  // only clustered launches stage halo rows in shared memory
+  const int smem = pl.cluster ? Gm::SMEM : Gm::SMEM - Gm::HALO;
+  return launch_dependent_c(kern, dim3(pl.ns, pairs), kThreads, smem, pl.cluster ? pl.ns : 1, st, A);
 }
 
 template <bool ATTEND, typename KT, typename VT, int D>
