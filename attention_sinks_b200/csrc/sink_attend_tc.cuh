@@ -66,7 +66,12 @@ struct TcArgs {
   int heads_kv, group, row_end, rows_per_split, ns, pairs;
   int q_async;            // qmap is valid: each item's q rows are prefetched by TMA
   float scale_log2;
+  // 1: one item per CTA and the ns CTAs of each pair launched as one cluster; the pair's
+  // split partials are merged at the end of the kernel (no sink_combine_kernel launch).
+  int cluster;
 };
+
+constexpr int kTcClusterMax = 8;  // one CTA per SM: portable cluster sizes only
 
 // ------------------------------------------------------------------ tcgen05 / TMA wrappers
 
@@ -611,6 +616,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols)
                  : "memory");
+  }
+  if (A.cluster) {
+    // Every CTA of the cluster has written its partial (the barrier's release/acquire makes
+    // them visible); each merges a slice of the pair's G * 128 outputs, as the combine
+    // kernel would.  Partials are read through L2 (.cg).
+    cluster_sync();
+    const int p = int(blockIdx.x) / A.ns, j = int(blockIdx.x) - p * A.ns;
+    const int b = p / A.heads_kv, h = p - b * A.heads_kv;
+    const size_t base = size_t(p) * A.ns;
+    for (int idx = j * kTcThreads + tid; idx < G * kTcD; idx += A.ns * kTcThreads) {
+      const int g = idx / kTcD, d = idx - g * kTcD;
+      float mx = kNegInf;
+      for (int s = 0; s < A.ns; ++s) mx = fmaxf(mx, __ldcg(A.m_part + (base + s) * G + g));
+      const float mref = mx == kNegInf ? 0.f : mx;
+      float sum = 0.f;
+      for (int s = 0; s < A.ns; ++s)
+        sum = __fmaf_rn(exp2f(__ldcg(A.m_part + (base + s) * G + g) - mref), __ldcg(A.l_part + (base + s) * G + g), sum);
+      const float inv = 1.f / sum;
+      float o = 0.f;
+      for (int s = 0; s < A.ns; ++s)
+        o = __fmaf_rn(exp2f(__ldcg(A.m_part + (base + s) * G + g) - mref) * inv,
+                      __ldcg(A.o_part + ((base + s) * G + g) * kTcD + d), o);
+      T* op = reinterpret_cast<T*>(A.out) + b * A.o_sb + (h * G + g) * A.o_sh;
+      op[d] = Elem<T>::from_f(o);
+    }
   }
 }
 

@@ -456,8 +456,19 @@ int32_t encode_query_map(CUtensorMap* map, const sink_rows_t* q, int batch, int 
   return r == CUDA_SUCCESS ? SINK_OK : SINK_ELAYOUT;
 }
 
+// Clusters of n tensor-core CTAs (one per SM) that fit the device at once, per device and n
+// (cudaOccupancyMaxActiveClusters, queried by prepare_device outside any capture).
+std::atomic<int> g_tc_clusters[64][kTcClusterMax + 1];
+
+// A split attention whose items all run at once (one per CTA) merges its partials inside
+// each pair's cluster when the device holds every such cluster together.
+bool tc_cluster_merge(int dev, int ns, long items, int sms) {
+  if (ns < 2 || ns > kTcClusterMax || items > sms || dev < 0 || dev >= 64) return false;
+  return items / ns <= g_tc_clusters[dev][ns].load(std::memory_order_relaxed);
+}
+
 template <typename T, int GMAX>
-int32_t launch_tc_g(const TcArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev) {
+int32_t launch_tc_g(const TcArgs& A0, const Plan& pl, int pairs, cudaStream_t st, int dev, bool* merged) {
   auto kern = sink_attend_tc_kernel<T, GMAX>;
   const int32_t rc = prepare_device(dev);
   if (rc) return rc;
@@ -465,15 +476,18 @@ int32_t launch_tc_g(const TcArgs& A, const Plan& pl, int pairs, cudaStream_t st,
   if (sms <= 0) return SINK_EDEVICE;
   const long items = long(pl.ns) * pairs;
   const int grid = int(items < sms ? items : sms);
-  return launch_dependent_n(kern, dim3(grid), kTcThreads, kTcSmemBytes, st, A);
+  TcArgs A = A0;
+  *merged = tc_cluster_merge(dev, pl.ns, items, sms);
+  A.cluster = *merged ? 1 : 0;
+  return launch_dependent_c(kern, dim3(grid), kTcThreads, kTcSmemBytes, *merged ? pl.ns : 1, st, A);
 }
 
 template <typename T>
-int32_t launch_tc_t(int G, const TcArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev) {
-  if (G <= 1) return launch_tc_g<T, 1>(A, pl, pairs, st, dev);
-  if (G <= 2) return launch_tc_g<T, 2>(A, pl, pairs, st, dev);
-  if (G <= 4) return launch_tc_g<T, 4>(A, pl, pairs, st, dev);
-  return launch_tc_g<T, 8>(A, pl, pairs, st, dev);
+int32_t launch_tc_t(int G, const TcArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev, bool* merged) {
+  if (G <= 1) return launch_tc_g<T, 1>(A, pl, pairs, st, dev, merged);
+  if (G <= 2) return launch_tc_g<T, 2>(A, pl, pairs, st, dev, merged);
+  if (G <= 4) return launch_tc_g<T, 4>(A, pl, pairs, st, dev, merged);
+  return launch_tc_g<T, 8>(A, pl, pairs, st, dev, merged);
 }
 
 int32_t launch_attention_tc(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows,
@@ -507,10 +521,11 @@ int32_t launch_attention_tc(const sink_rows_t* q, const sink_kv_buffers_t* kv, i
   A.scale_log2 = scale * kLog2e;
   const int pairs = kv->batch * kv->heads_kv;
   A.pairs = pairs;
-  rc = kv->k_dtype == SINK_DTYPE_BF16 ? launch_tc_t<__nv_bfloat16>(A.group, A, pl, pairs, st, dev)
-                                      : launch_tc_t<__half>(A.group, A, pl, pairs, st, dev);
+  bool merged = false;
+  rc = kv->k_dtype == SINK_DTYPE_BF16 ? launch_tc_t<__nv_bfloat16>(A.group, A, pl, pairs, st, dev, &merged)
+                                      : launch_tc_t<__half>(A.group, A, pl, pairs, st, dev, &merged);
   if (rc) return rc;
-  if (pl.ns > 1) {
+  if (pl.ns > 1 && !merged) {
     StreamArgs C;
     std::memset(&C, 0, sizeof(C));
     C.o_part = A.o_part;
@@ -733,6 +748,31 @@ cudaError_t allow_smem_tc() {
 
 std::atomic<uint64_t> g_prepared{0};  // one bit per device
 
+// How many clusters of n tensor-core CTAs the device holds at once (0 when the query fails:
+// that size is then never clustered).
+void tc_cluster_capacity(int dev) {
+  if (dev < 0 || dev >= 64) return;
+  for (int n = 2; n <= kTcClusterMax; ++n) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(n));
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = kTcSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(n);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, sink_attend_tc_kernel<__nv_bfloat16, 2>, &cfg) != cudaSuccess) {
+      clusters = 0;
+      (void)cudaGetLastError();
+    }
+    g_tc_clusters[dev][n].store(clusters, std::memory_order_relaxed);
+  }
+}
+
 int32_t prepare_device(int dev) {
   const uint64_t bit = uint64_t(1) << dev;
   if (g_prepared.load(std::memory_order_acquire) & bit) return SINK_OK;
@@ -741,6 +781,7 @@ int32_t prepare_device(int dev) {
   if (e == cudaSuccess) e = allow_smem_tc<__nv_bfloat16>();
   if (e == cudaSuccess) e = allow_smem_tc<__half>();
   if (e != cudaSuccess) return e;
+  tc_cluster_capacity(dev);
   if (tensor_map_encoder() == nullptr) return SINK_EDEVICE;
   g_prepared.fetch_or(bit, std::memory_order_acq_rel);
   return SINK_OK;
