@@ -71,7 +71,9 @@ struct TcArgs {
   int cluster;
 };
 
-constexpr int kTcClusterMax = 8;  // one CTA per SM: portable cluster sizes only
+// Largest cluster (a pair's splits) for the in-cluster merge; sizes above 8 are used only
+// where the device's occupancy query says every such cluster fits at once.
+constexpr int kTcClusterMax = 16;
 
 // ------------------------------------------------------------------ tcgen05 / TMA wrappers
 

@@ -14,10 +14,14 @@ namespace sinkb200 {
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr float kNegInf = -__builtin_inff();
 
-template <typename KT, typename VT, int D, int GMAX, bool ATTEND>
+// NW warps per CTA share each chunk: warp w takes row groups w, w + NW, ... (T / (NW * RPW)
+// steps of RPW rows).  The chunk geometry (T rows) does not depend on NW.
+template <typename KT, typename VT, int D, int GMAX, bool ATTEND, int NW = kWarps>
 struct StreamLanes {
   using Gm = StreamGeom<KT, VT, D>;
-  static constexpr int LPR = Gm::LPR, RPW = Gm::RPW, STEPS = Gm::STEPS;
+  static constexpr int LPR = Gm::LPR, RPW = Gm::RPW;
+  static constexpr int STEPS = Gm::T / (NW * RPW);
+  static_assert(STEPS * NW * RPW == Gm::T && STEPS >= 1, "warps per chunk");
   static constexpr int NG = ATTEND ? GMAX : 1;
 
   int warp, lane, li, rg;
@@ -79,7 +83,7 @@ struct StreamLanes {
     float sc[NG][STEPS];
 #pragma unroll
     for (int i = 0; i < STEPS; ++i) {
-      const int t = i * (kWarps * RPW) + warp * RPW + rg;
+      const int t = i * (NW * RPW) + warp * RPW + rg;
       const int r = x + t;
       const bool valid = r < xe;
       float lo[4], hi[4];
@@ -140,7 +144,7 @@ struct StreamLanes {
       }
 #pragma unroll
       for (int i = 0; i < STEPS; ++i) {
-        const int t = i * (kWarps * RPW) + warp * RPW + rg;
+        const int t = i * (NW * RPW) + warp * RPW + rg;
         if (x + t < xe) {
           float v[8];
           Elem<VT>::load8(sv + t * D + 8 * li, v);
@@ -155,7 +159,7 @@ struct StreamLanes {
   }
 
   // Scratch floats the warp merge needs.
-  static constexpr int kScratchFloats = kWarps * GMAX * (D + 2);
+  static constexpr int kScratchFloats = NW * GMAX * (D + 2);
 
   // Reduce the row groups of each warp and write (m, l, acc) of every warp to `scratch`.
   // The caller synchronises the CTA before reading the scratch back.
@@ -171,8 +175,8 @@ struct StreamLanes {
         }
       }
       float* sm_m = scratch;
-      float* sm_l = sm_m + kWarps * GMAX;
-      float* sm_acc = sm_l + kWarps * GMAX;
+      float* sm_l = sm_m + NW * GMAX;
+      float* sm_acc = sm_l + NW * GMAX;
       if (lane < LPR) {
 #pragma unroll
         for (int g = 0; g < GMAX; ++g) {
@@ -195,16 +199,16 @@ struct StreamLanes {
   static __device__ __forceinline__ void from_scratch(const float* scratch, int g, int d, float& M,
                                                       float& L, float& O) {
     const float* sm_m = scratch;
-    const float* sm_l = sm_m + kWarps * GMAX;
-    const float* sm_acc = sm_l + kWarps * GMAX;
+    const float* sm_l = sm_m + NW * GMAX;
+    const float* sm_acc = sm_l + NW * GMAX;
     M = kNegInf;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm_m[w * GMAX + g]);
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w * GMAX + g]);
     const float Mref = M == kNegInf ? 0.f : M;
     L = 0.f;
     O = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
+    for (int w = 0; w < NW; ++w) {
       const float wt = exp2f(sm_m[w * GMAX + g] - Mref);
       L = __fmaf_rn(wt, sm_l[w * GMAX + g], L);
       O = __fmaf_rn(wt, sm_acc[(w * GMAX + g) * D + d], O);

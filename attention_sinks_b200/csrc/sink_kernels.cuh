@@ -80,33 +80,37 @@ __device__ __forceinline__ void store_range(const StreamArgs& A, int x, int xe, 
 }
 
 // The new token's K/V row into stage row t (converted to the key storage type).
-template <typename KT, typename VT, int D>
+template <typename KT, typename VT, int D, int NT = kThreads>
 __device__ __forceinline__ void fill_append_row(const StreamArgs& A, int b, int h, KT* sk, VT* sv, int t) {
   const VT* kn = reinterpret_cast<const VT*>(A.knew) + b * A.kn_sb + h * A.kn_sh;
   const VT* vn = reinterpret_cast<const VT*>(A.vnew) + b * A.vn_sb + h * A.vn_sh;
-  for (int d = threadIdx.x; d < D; d += kThreads) {
+  for (int d = threadIdx.x; d < D; d += NT) {
     sk[t * D + d] = Elem<KT>::from_f(Elem<VT>::to_f(kn[d]));
     sv[t * D + d] = vn[d];
   }
 }
 
 // Copy n rows (K and V) between shared-memory row arrays, 16 bytes per thread-step.
-template <int KROW, int VROW>
+template <int KROW, int VROW, int NT = kThreads>
 __device__ __forceinline__ void copy_rows(unsigned char* dk, unsigned char* dv, const unsigned char* sk,
                                           const unsigned char* sv, int n) {
   const int nk = n * KROW / 16, nv = n * VROW / 16;
-  for (int i = threadIdx.x; i < nk; i += kThreads)
+  for (int i = threadIdx.x; i < nk; i += NT)
     reinterpret_cast<uint4*>(dk)[i] = reinterpret_cast<const uint4*>(sk)[i];
-  for (int i = threadIdx.x; i < nv; i += kThreads)
+  for (int i = threadIdx.x; i < nv; i += NT)
     reinterpret_cast<uint4*>(dv)[i] = reinterpret_cast<const uint4*>(sv)[i];
 }
 
 // ============================================================================ split
 
-template <typename KT, typename VT, int D, int GMAX, bool ATTEND>
-__global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_constant__ StreamArgs A) {
+// NW warps per CTA (4; 8 for clustered launches, where a CTA is usually alone on its SM and
+// its chunk latency, not memory, bounds the step).
+template <typename KT, typename VT, int D, int GMAX, bool ATTEND, int NW>
+__global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_constant__ StreamArgs A) {
+  constexpr int NT = 32 * NW;
   using Gm = StreamGeom<KT, VT, D>;
-  using Lanes = StreamLanes<KT, VT, D, GMAX, ATTEND>;
+  using Lanes = StreamLanes<KT, VT, D, GMAX, ATTEND, NW>;
+  static_assert((NW + 1) * GMAX * (D + 2) * 4 <= Gm::S * Gm::STAGE, "merge scratch");
   constexpr int T = Gm::T, S = Gm::S, KROW = Gm::KROW, STAGE = Gm::STAGE;
   constexpr int VROW = Gm::VROW;
 
@@ -187,13 +191,13 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
     KT* sk = reinterpret_cast<KT*>(stages + stage * STAGE);
     VT* sv = reinterpret_cast<VT*>(stages + stage * STAGE + T * KROW);
     if (A.append_row >= x && A.append_row < xe) {  // CTA-uniform
-      fill_append_row<KT, VT, D>(A, b, h, sk, sv, A.append_row - x);
+      fill_append_row<KT, VT, D, NT>(A, b, h, sk, sv, A.append_row - x);
       __syncthreads();
     }
     if (clustered && has_halo) {  // output rows whose sources are the staged halo rows
       const int r0 = imax(x, hlo - A.drop), r1 = imin(xe, hhi - A.drop);
       if (r0 < r1) {  // CTA-uniform
-        copy_rows<KROW, VROW>(reinterpret_cast<unsigned char*>(sk) + (r0 - x) * KROW,
+        copy_rows<KROW, VROW, NT>(reinterpret_cast<unsigned char*>(sk) + (r0 - x) * KROW,
                               reinterpret_cast<unsigned char*>(sv) + (r0 - x) * VROW,
                               halo_sk + (r0 + A.drop - hlo) * KROW, halo_sv + (r0 + A.drop - hlo) * VROW,
                               r1 - r0);
@@ -231,7 +235,7 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
     __syncthreads();
     const int G = A.group;
     if (!clustered) {
-      for (int idx = tid; idx < G * D; idx += kThreads) {
+      for (int idx = tid; idx < G * D; idx += NT) {
         const int g = idx / D, d = idx - g * D;
         float M, Ls, O;
         Lanes::from_scratch(scratch, g, d, M, Ls, O);
@@ -251,8 +255,8 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
     }
     // Clustered: this CTA's partial (O[g][d], then M[g], L[g]) stays in shared memory; after
     // the barrier every CTA merges a slice of the pair's G * D outputs from all ns partials.
-    float* part = scratch + kWarps * GMAX * (D + 2);
-    for (int idx = tid; idx < G * D; idx += kThreads) {
+    float* part = scratch + NW * GMAX * (D + 2);
+    for (int idx = tid; idx < G * D; idx += NT) {
       const int g = idx / D, d = idx - g * D;
       float M, Ls, O;
       Lanes::from_scratch(scratch, g, d, M, Ls, O);
@@ -265,7 +269,7 @@ __global__ void __launch_bounds__(kThreads) sink_stream_kernel(const __grid_cons
     cluster_sync();
     if (!failed) {
       const uint32_t part_addr = smem_addr(part);
-      for (int idx = j * kThreads + tid; idx < G * D; idx += A.ns * kThreads) {
+      for (int idx = j * NT + tid; idx < G * D; idx += A.ns * NT) {
         const int g = idx / D, d = idx - g * D;
         float mx = kNegInf;
         for (int r = 0; r < A.ns; ++r)

@@ -72,13 +72,18 @@ void geometry_tc(Plan& pl) {
 }
 
 // Split plan: every (batch, head) pair's rows cut into `ns` items of `tps` chunks, one CTA
-// each.  Two regimes, from measurements over the op-bench grid on B200:
+// each.  Regimes, from measurements over the op-bench grid on B200:
 //   - a step whose pairs fit in one wave of CTAs with items of at most kMaxItemChunks
 //     chunks takes exactly one wave: as many splits per pair as there are free SM slots
 //     per pair (few pairs with long rows: every SM streams one long item);
+//   - (stream kernel) pairs that alone fill the CTA slots, with rows that fit one item,
+//     take one split each: no halo pre-pass, no combine (256 slots x 64 streams: 57.5 ->
+//     43.1 us);
 //   - otherwise items of kMinItemChunks..kMaxItemChunks chunks, aiming at kTargetWaves
-//     waves, so the block scheduler evens out SMs that stream at different rates.
-constexpr long kMinItemChunks = 4;
+//     waves, so the block scheduler evens out SMs that stream at different rates.  Items
+//     shorter than 8 chunks spend too much of their time filling the pipeline (4 -> 8:
+//     1,024 x 64 159.5 -> 143.8 us, 4,096 x 8 94.4 -> 87.8 us, no grid point slower).
+constexpr long kMinItemChunks = 8;
 constexpr long kMaxItemChunks = 32;
 constexpr long kTargetWaves = 16;
 // The persistent tensor-core kernel streams its items back to back, so it wants more,
@@ -86,12 +91,15 @@ constexpr long kTargetWaves = 16;
 constexpr long kTcTargetItemsPerCta = 64;
 constexpr long kTcMinItemChunks = 2;
 
-void choose_splits(int pairs, int rows, int T, int slots, long target_waves, long min_chunks, Plan& pl) {
+void choose_splits(int pairs, int rows, int T, int slots, long target_waves, long min_chunks,
+                   bool single_when_full, Plan& pl) {
   const long tiles = (rows + T - 1) / T;
   const long total = long(pairs) * tiles;
   long ns;
   if (long(pairs) * ((tiles + kMaxItemChunks - 1) / kMaxItemChunks) <= slots) {
     ns = slots / pairs;
+  } else if (single_when_full && pairs >= slots && tiles <= kMaxItemChunks) {
+    ns = 1;
   } else {
     long tps = (total + target_waves * slots - 1) / (target_waves * slots);
     tps = tps < min_chunks ? min_chunks : (tps > kMaxItemChunks ? kMaxItemChunks : tps);
@@ -156,9 +164,9 @@ int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
   if (nrows < 1) return SINK_EINVAL;
   const int pairs = batch * heads_kv;
   if (pl.tc)
-    choose_splits(pairs, nrows, pl.T, num_sms, kTcTargetItemsPerCta, kTcMinItemChunks, pl);
+    choose_splits(pairs, nrows, pl.T, num_sms, kTcTargetItemsPerCta, kTcMinItemChunks, false, pl);
   else {
-    choose_splits(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, kTargetWaves, kMinItemChunks, pl);
+    choose_splits(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, kTargetWaves, kMinItemChunks, true, pl);
     choose_cluster(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, drop, pl);
   }
   size_t off = 256;  // status word
@@ -266,17 +274,29 @@ int32_t launch_dependent(void (*kern)(Params...), dim3 grid, int smem, cudaStrea
   return launch_dependent_n(kern, grid, kThreads, smem, st, args...);
 }
 
+// Warps per CTA of a clustered stream launch: 8, or 4 where the merge scratch of 8 warps
+// (plus the CTA partial) does not fit the stage memory (16-bit K and V with head_dim 256).
+template <typename KT, typename VT, int D, int GMAX>
+constexpr int cluster_warps() {
+  using Gm = StreamGeom<KT, VT, D>;
+  return 9 * GMAX * (D + 2) * 4 <= Gm::S * Gm::STAGE ? 8 : 4;
+}
+
 template <typename KT, typename VT, int D, int GMAX, bool ATTEND>
 int32_t launch_stream(const StreamArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev) {
   using Gm = StreamGeom<KT, VT, D>;
   if (Gm::SMEM != pl.smem || Gm::T != pl.T) return SINK_EINVAL;  // host/device geometry drift
-  auto kern = sink_stream_kernel<KT, VT, D, GMAX, ATTEND>;
+  // clustered launches (one CTA per SM in the latency regime) run 8 warps per CTA where the
+  // merge scratch of 8 warps fits the stage memory
+  constexpr int NWC = cluster_warps<KT, VT, D, GMAX>();
+  auto kern = pl.cluster ? sink_stream_kernel<KT, VT, D, GMAX, ATTEND, NWC> : sink_stream_kernel<KT, VT, D, GMAX, ATTEND, 4>;
+  const int threads = pl.cluster ? 32 * NWC : kThreads;
   const int32_t rc = prepare_device(dev);
   if (rc) return rc;
   if (pl.cluster && (pl.ns > kClusterMax || A.cluster != 1)) return SINK_EINVAL;
   // only clustered launches stage halo rows in shared memory
   const int smem = pl.cluster ? Gm::SMEM : Gm::SMEM - Gm::HALO;
-  return launch_dependent_c(kern, dim3(pl.ns, pairs), kThreads, smem, pl.cluster ? pl.ns : 1, st, A);
+  return launch_dependent_c(kern, dim3(pl.ns, pairs), threads, smem, pl.cluster ? pl.ns : 1, st, A);
 }
 
 template <bool ATTEND, typename KT, typename VT, int D>
@@ -694,13 +714,13 @@ int32_t launch_v2_place(const sink_kv_buffers_t* kv, const V2PlaceArgs& a, int s
 // Opt every kernel that uses more than 48 KB of dynamic shared memory into its size, and
 // look up the tensor-map encoder: calls that must not happen inside a stream capture, so
 // they are made once per device, by sink_prepare_device() or by the first launch.
-// A stream kernel's dynamic shared memory, and clusters of up to 16 CTAs (above the portable
-// 8; B200 schedules 16 of these 2-per-SM CTAs on one GPC).
+// A kernel's dynamic shared memory, and clusters of up to 16 CTAs (above the portable 8;
+// B200 schedules 16 of the stream kernel's 2-per-SM CTAs on one GPC; for the one-per-SM
+// tensor-core kernel the occupancy query decides).
 template <typename... Params>
 cudaError_t stream_attrs(void (*kern)(Params...), int bytes) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess && kClusterMax > 8)
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   return e;
 }
 
@@ -708,12 +728,19 @@ template <bool ATTEND, typename KT, typename VT, int D>
 cudaError_t allow_smem_d() {
   const int bytes = StreamGeom<KT, VT, D>::SMEM;
   if constexpr (!ATTEND) {
-    return stream_attrs(sink_stream_kernel<KT, VT, D, 1, false>, bytes);
+    cudaError_t e = stream_attrs(sink_stream_kernel<KT, VT, D, 1, false, 4>, bytes);
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 1, false, cluster_warps<KT, VT, D, 1>()>, bytes);
+    return e;
   } else {
-    cudaError_t e = stream_attrs(sink_stream_kernel<KT, VT, D, 1, true>, bytes);
-    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 2, true>, bytes);
-    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 4, true>, bytes);
-    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 8, true>, bytes);
+    cudaError_t e = cudaSuccess;
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 1, true, 4>, bytes);
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 2, true, 4>, bytes);
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 4, true, 4>, bytes);
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 8, true, 4>, bytes);
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 1, true, cluster_warps<KT, VT, D, 1>()>, bytes);
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 2, true, cluster_warps<KT, VT, D, 2>()>, bytes);
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 4, true, cluster_warps<KT, VT, D, 4>()>, bytes);
+    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 8, true, cluster_warps<KT, VT, D, 8>()>, bytes);
     return e;
   }
 }
@@ -739,10 +766,10 @@ cudaError_t allow_smem_stream() {
 template <typename T>
 cudaError_t allow_smem_tc() {
   const int b = kTcSmemBytes;
-  cudaError_t e = cudaFuncSetAttribute(sink_attend_tc_kernel<T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(sink_attend_tc_kernel<T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(sink_attend_tc_kernel<T, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(sink_attend_tc_kernel<T, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+  cudaError_t e = stream_attrs(sink_attend_tc_kernel<T, 1>, b);
+  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 2>, b);
+  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 4>, b);
+  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 8>, b);
   return e;
 }
 

@@ -192,8 +192,9 @@ class OpBench:
                               N_SINK, self.window, 1, sms)
 
     def launches_per_step(self) -> int:
-        ns = self.plan["splits"]
-        return 1 + (2 if ns > 1 else 0)  # halo pre-pass and split combine when split
+        if self.plan["splits"] == 1 or self.plan["cluster_ctas"] > 1:
+            return 1  # one split, or every split of a pair in one cluster: a single launch
+        return 3  # halo pre-pass, stream kernel, split combine
 
     def step(self, i: int) -> None:
         j = i % self.POOL
