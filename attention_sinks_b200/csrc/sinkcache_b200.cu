@@ -87,8 +87,10 @@ constexpr long kMinItemChunks = 8;
 constexpr long kMaxItemChunks = 32;
 constexpr long kTargetWaves = 16;
 // The persistent tensor-core kernel streams its items back to back, so it wants more,
-// smaller items (about 64 per CTA) to even out the last round.
-constexpr long kTcTargetItemsPerCta = 64;
+// smaller items to even out the last round: about 16 per CTA.  (64 per CTA left items of
+// 2 chunks at 32,768 slots x 8 streams, where each item's Q load, epilogue and partial
+// cost more than the balance gained: 212 -> 184 us; no grid point slower.)
+constexpr long kTcTargetItemsPerCta = 16;
 constexpr long kTcMinItemChunks = 2;
 
 void choose_splits(int pairs, int rows, int T, int slots, long target_waves, long min_chunks,
