@@ -6,9 +6,12 @@
 //                        stores, and (ATTEND) a GQA online-softmax decode attention runs over
 //                        the same rows.  With drop == 0 and no append row it is a plain
 //                        split-K decode attention; with ATTEND == false a plain eviction.
+//                        Launched as one cluster per pair (StreamArgs::cluster), it stages
+//                        its halo rows in shared memory and merges the split partials
+//                        across the cluster itself: the whole step in one launch.
 //   sink_halo_kernel     copies the source rows a later split overwrites before an earlier
-//                        split reads them (pre-pass of an in-place shift).
-//   sink_combine_kernel  merges the per-split softmax partials.
+//                        split reads them (pre-pass of an unclustered in-place shift).
+//   sink_combine_kernel  merges the per-split softmax partials (unclustered launches).
 //   sink_append_kernel   writes new K/V rows (unfused path).
 #pragma once
 

@@ -186,7 +186,10 @@ int32_t sink_read_status(void* workspace, void* stream, int32_t* status);
 
 /*
  * One-time set-up of the current device: opts the kernels into their shared-memory sizes
- * and looks up the driver's tensor-map encoder.  These calls cannot be made inside a CUDA
+ * and cluster sizes, asks the device how many clusters of the tensor-core attention kernel
+ * it holds at once (which decides, at launch, whether a split attention merges its
+ * partials inside clusters), and looks up the driver's tensor-map encoder.  These calls
+ * cannot be made inside a CUDA
  * stream capture, so call this once per device before capturing any launch of this
  * library into a graph (every entry point also runs it on its first use).  No counterpart
  * in the reference (its Triton kernels compile on first use instead).
