@@ -33,6 +33,7 @@ def _cluster(op, batch, hkv, hq, d, kdt, vdt, rows, n_sink, window, drop):
     (2, 32, 8, 64, 700, 4, torch.bfloat16),
     (3, 24, 3, 256, 200, 2, torch.float16),
     (2, 8, 8, 128, 333, 0, torch.bfloat16),
+    (1, 64, 8, 128, 2047, 4, torch.bfloat16),  # GQA group 8: one CTA per SM, a 16-CTA cluster
 ])
 def test_clustered_fused_step(batch, hq, hkv, d, slots, n_sink, vdt, built_lib):
     """One steady decode step on a clustered launch: cache bit for bit, output within 2e-2."""
