@@ -79,6 +79,8 @@ void geometry_tc(Plan& pl) {
 //   - (stream kernel) pairs that alone fill the CTA slots, with rows that fit one item,
 //     take one split each: no halo pre-pass, no combine (256 slots x 64 streams: 57.5 ->
 //     43.1 us);
+//   - (stream kernel) a plan of fewer than kFewWaves waves: the item size of
+//     few_wave_item_chunks;
 //   - otherwise items of kMinItemChunks..kMaxItemChunks chunks, aiming at kTargetWaves
 //     waves, so the block scheduler evens out SMs that stream at different rates.  Items
 //     shorter than 8 chunks spend too much of their time filling the pipeline (4 -> 8:
@@ -93,18 +95,42 @@ constexpr long kTargetWaves = 16;
 constexpr long kTcTargetItemsPerCta = 16;
 constexpr long kTcMinItemChunks = 2;
 
+// A stream-kernel plan of fewer than kFewWaves waves picks its item size by
+// ceil(waves) * (chunks per item + kFillChunks): with so few waves the last one's fill
+// matters, and a CTA spends about kFillChunks chunks' time filling its pipeline.  (4,096
+// slots x 8 streams: 17 splits of 8 chunks, 3.7 waves, 87.8 us -> 9 splits of 15, 1.95
+// waves, 79.9 us.  Over more waves the scheduler overlaps them and the model misleads.)
+constexpr long kFewWaves = 4;
+constexpr long kFillChunks = 3;
+
+long few_wave_item_chunks(long pairs, long tiles, long slots, long min_chunks, long tps) {
+  long best = tps, best_cost = LONG_MAX;
+  for (long c = min_chunks; c <= kMaxItemChunks; ++c) {
+    const long n = (tiles + c - 1) / c;
+    const long waves = (pairs * n + slots - 1) / slots;
+    const long cost = waves * ((tiles + n - 1) / n + kFillChunks);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = c;
+    }
+  }
+  return best;
+}
+
 void choose_splits(int pairs, int rows, int T, int slots, long target_waves, long min_chunks,
-                   bool single_when_full, Plan& pl) {
+                   bool stream_rules, Plan& pl) {
   const long tiles = (rows + T - 1) / T;
   const long total = long(pairs) * tiles;
   long ns;
   if (long(pairs) * ((tiles + kMaxItemChunks - 1) / kMaxItemChunks) <= slots) {
     ns = slots / pairs;
-  } else if (single_when_full && pairs >= slots && tiles <= kMaxItemChunks) {
+  } else if (stream_rules && pairs >= slots && tiles <= kMaxItemChunks) {
     ns = 1;
   } else {
     long tps = (total + target_waves * slots - 1) / (target_waves * slots);
     tps = tps < min_chunks ? min_chunks : (tps > kMaxItemChunks ? kMaxItemChunks : tps);
+    if (stream_rules && long(pairs) * ((tiles + tps - 1) / tps) < kFewWaves * slots)
+      tps = few_wave_item_chunks(pairs, tiles, slots, min_chunks, tps);
     ns = (tiles + tps - 1) / tps;
   }
   if (ns > tiles) ns = tiles;

@@ -88,7 +88,7 @@ def test_plan_covers_rows_exactly(op, rows, n_sink, window, drop, batch, kdt):
 
 @pytest.mark.parametrize("batch,slots,ns,clustered", [
     (1, 256, 9, True), (1, 1024, 11, True), (2, 4096, 15, True), (4, 4096, 9, True), (8, 1024, 4, True),
-    (1, 4096, 33, False), (64, 256, 1, False), (1, 32768, 37, False), (8, 4096, 17, False),
+    (1, 4096, 33, False), (64, 256, 1, False), (1, 32768, 37, False), (8, 4096, 9, False),
     (64, 32768, 33, False),
 ])
 def test_plan_clusters_small_steps(batch, slots, ns, clustered, built_lib):
