@@ -152,18 +152,29 @@ void choose_splits(int pairs, int rows, int T, int slots, long target_waves, lon
 // kClusterHaloRows rows keeps the halo pre-pass.
 constexpr long kClusterExtraChunks = 4;
 
+// Clusters of more than kClusterPortable CTAs only for splits of at most
+// kLargeClusterChunks chunks: measured on one-wave steps with more bytes to stream, large
+// clusters lose 27-31 % against the split launch (8,192 slots x 4 streams, 9 CTAs of 29
+// chunks: 111.9 -> 78.5 us unclustered; 4,096 x 2, 15 of 9: 47.2 -> 34.3 us), while
+// clusters of 4-5 CTAs win even with 17-26 chunk splits (2,048 x 8: 40.9 against 46.1 us).
+constexpr long kClusterPortable = 8;
+constexpr long kLargeClusterChunks = 4;
+
 void choose_cluster(int pairs, int rows, int T, int slots, int drop, Plan& pl) {
   if (drop > kClusterHaloRows || pl.ns < 2) return;
   const long tiles = (rows + T - 1) / T;
   if (long(pairs) * pl.ns > slots) return;
-  if (pl.ns > kClusterMax) {
-    const long tps0 = pl.rows_per_split / T;
-    const long tps = (tiles + kClusterMax - 1) / kClusterMax;
+  long ns = pl.ns, tps = pl.rows_per_split / T;
+  if (ns > kClusterMax) {
+    const long tps0 = tps;
+    tps = (tiles + kClusterMax - 1) / kClusterMax;
     if (tps > kMaxItemChunks || tps - tps0 > kClusterExtraChunks) return;
-    pl.ns = int((tiles + tps - 1) / tps);
-    pl.rows_per_split = int(tps) * T;
+    ns = (tiles + tps - 1) / tps;
   }
-  pl.cluster = pl.ns > 1;
+  if (ns > kClusterPortable && tps > kLargeClusterChunks) return;
+  pl.ns = int(ns);
+  pl.rows_per_split = int(tps) * T;
+  pl.cluster = ns > 1;
 }
 
 int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, int32_t D,

@@ -87,15 +87,16 @@ def test_plan_covers_rows_exactly(op, rows, n_sink, window, drop, batch, kdt):
 
 
 @pytest.mark.parametrize("batch,slots,ns,clustered", [
-    (1, 256, 9, True), (1, 1024, 11, True), (2, 4096, 15, True), (4, 4096, 9, True), (8, 1024, 4, True),
+    (1, 256, 9, True), (1, 1024, 11, True), (2, 2047, 16, True), (7, 4096, 5, True), (8, 1024, 4, True),
+    (2, 4096, 17, False), (4, 4096, 9, False), (2, 8192, 18, False), (4, 8192, 9, False),
     (1, 4096, 33, False), (64, 256, 1, False), (1, 32768, 37, False), (8, 4096, 9, False),
     (64, 32768, 33, False),
 ])
 def test_plan_clusters_small_steps(batch, slots, ns, clustered, built_lib):
     """Fused steps whose CTAs fit one wave with at most 16 splits per pair (or 16 splits
     that add at most 4 chunks per split) run as one clustered launch: no halo or partials
-    workspace.  Several waves, or longer splits, keep the split launch with its halo
-    pre-pass and combine."""
+    workspace.  Clusters of more than 8 CTAs only for splits of at most 4 chunks.  Several
+    waves, or longer splits, keep the split launch with its halo pre-pass and combine."""
     f32, bf16 = torch.float32, torch.bfloat16
     args = (_lib.OP_FUSED_STEP, batch, 8, 16, 128, f32, bf16, slots + 1, 4, slots - 4, 1, 148)
     p = _lib.plan(*args)

@@ -28,7 +28,7 @@ def _cluster(op, batch, hkv, hq, d, kdt, vdt, rows, n_sink, window, drop):
     (1, 16, 8, 128, 64, 4, torch.bfloat16),
     (1, 16, 8, 128, 256, 4, torch.bfloat16),
     (1, 16, 8, 128, 1024, 4, torch.bfloat16),
-    (2, 16, 8, 128, 4096, 4, torch.bfloat16),
+    (2, 16, 8, 128, 2047, 4, torch.bfloat16),
     (8, 16, 8, 128, 1024, 4, torch.bfloat16),
     (2, 32, 8, 64, 700, 4, torch.bfloat16),
     (3, 24, 3, 256, 200, 2, torch.float16),
