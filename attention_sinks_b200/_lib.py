@@ -24,9 +24,11 @@ EXPORTED_SYMBOLS = (
     "sink_abi_version", "sink_strerror", "sink_workspace_bytes", "sink_plan", "sink_append",
     "sink_evict_rerotate", "sink_decode_attention", "sink_fused_decode_step", "sink_read_status",
     "sink_decode_attention_noalloc", "sink_v2_place", "sink_v2_decode_step", "sink_prepare_device",
+    "sink_debug_fail_next_wait",
 )
 NOALLOC_SCRATCH_BYTES = 16 << 20
-ESCRATCH = -8
+# argument errors (negative return codes of the C ABI)
+EINVAL, EDTYPE, EHEADDIM, EGROUP, ELAYOUT, EWORKSPACE, EDEVICE, ESCRATCH = -1, -2, -3, -4, -5, -6, -7, -8
 
 
 class KVBuffers(ctypes.Structure):
@@ -70,6 +72,7 @@ def _declare(lib):
                                          ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
         "sink_read_status": (i32, [vp, vp, pi32]),
         "sink_prepare_device": (i32, []),
+        "sink_debug_fail_next_wait": (i32, [i32, i32]),
         "sink_decode_attention_noalloc": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, vp, i64, i64, vp]),
         "sink_v2_place": (i32, [pkv, prows, prows, prows, vp, i32, prows, vp, i64, i32, i32, vp, i32, vp]),
         "sink_v2_decode_step": (i32, [pkv, prows, prows, prows, vp, i32, vp, i32, i32, vp, i32, prows,
@@ -221,8 +224,25 @@ class Workspace:
                                       ctypes.byref(st)), "sink_read_status")
         return st.value
 
+    def check(self) -> None:
+        """Raise if a kernel reported a failure since the last read (synchronises the stream).
+        A bounded wait that ran out means the launches since then produced no valid result
+        and may have left an in-place eviction partly applied."""
+        status = self.read_status()
+        if status:
+            what = "a bounded wait for a bulk copy ran out" if status & STATUS_WAIT_TIMEOUT else "unknown failure"
+            raise RuntimeError(f"sinkcache_b200 kernel status 0x{status:x}: {what}; the results of the launches "
+                               "since the last check are void")
+
 
 # ---------------------------------------------------------------------------- operations
+
+
+def fail_next_wait(chunk: int, polls: int) -> None:
+    """Failure-detection test hook (sink_debug_fail_next_wait): the next stream-kernel launch
+    leaves chunk `chunk` of every split unissued, with every wait bounded by `polls` polls,
+    so that wait runs out and the launch reports SINK_STATUS_WAIT_TIMEOUT."""
+    _check(lib().sink_debug_fail_next_wait(int(chunk), int(polls)), "sink_debug_fail_next_wait")
 
 
 def append(kbuf: torch.Tensor, vbuf: torch.Tensor, k: torch.Tensor, v: torch.Tensor, row: int) -> None:

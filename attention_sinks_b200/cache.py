@@ -315,6 +315,11 @@ class SinkCache(Cache):
     def tokens_seen(self) -> int:
         return self.layers[0].tokens_seen
 
+    def check_status(self) -> None:
+        """Raise RuntimeError if one of this cache's kernels reported a failure (a bounded wait
+        for a bulk copy that ran out) since the last check; synchronises the stream."""
+        self.workspace.check()
+
     @property
     def tokens_evicted(self) -> int:
         return self.layers[0].tokens_evicted

@@ -65,6 +65,12 @@ struct StreamArgs {
   // through distributed shared memory: no halo pre-pass, no combine kernel, no workspace
   // beyond the status word.
   int cluster;
+  // Polls of each bounded mbarrier wait before it gives up (kWaitPolls unless a
+  // failure-detection test shortens it).
+  int wait_polls;
+  // Failure-detection test hook, -1 when off: every CTA leaves its chunk `skip_chunk`
+  // unissued (no copy, no arrival), so the wait for it runs out with nothing in flight.
+  int skip_chunk;
 };
 
 // Rows [a, e) of split j.
@@ -125,11 +131,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Default poll limit of a bounded wait: about a second with the back-off below.
+constexpr int kWaitPolls = 1 << 20;
+
 // Bounded wait for a phase of an mbarrier: false if the copies never landed (then the
 // caller records SINK_STATUS_WAIT_TIMEOUT and abandons its work instead of hanging).
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int polls = kWaitPolls) {
 #pragma unroll 1
-  for (int i = 0; i < (1 << 20); ++i) {
+  for (int i = 0; i < polls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (i >= 64) __nanosleep(256);
   }

@@ -155,14 +155,22 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
   }
   __syncthreads();
 
+  // Chunks whose loads thread 0 has issued, and chunks whose arrival it has seen: on a
+  // failure, the loads in between are waited for (bounded) before the CTA leaves, so no
+  // copy into this CTA's shared memory is still in flight when it exits.
+  int issued = 0, consumed = 0;
+  const int polls = A.wait_polls;
   auto issue_chunk = [&](int c) {
+    issued = c + 1;
+    if (c == A.skip_chunk) return;  // failure-detection test: leave this chunk unissued
     const int x = a + c * T, xe = imin(x + T, e);
     const uint32_t sk = smem_addr(stages + (c % S) * STAGE);
     issue_rows<KT, VT, D>(A, kb, vb, x, xe, hlo, hhi, hk, hv, sk, sk + T * KROW, bar0 + 8 * (c % S));
   };
 
+  const bool halo_issued = clustered && has_halo;
   if (tid == 0) {
-    if (clustered && has_halo) {  // hhi - hlo <= drop <= kClusterHaloRows rows (host-checked)
+    if (halo_issued) {  // hhi - hlo <= drop <= kClusterHaloRows rows (host-checked)
       const uint32_t n = uint32_t(hhi - hlo);
       mbar_arrive_expect_tx(halo_bar, n * (KROW + VROW));
       bulk_g2s(smem_addr(halo_sk), kb + size_t(hlo) * D, n * KROW, halo_bar);
@@ -172,12 +180,15 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
     for (int c = 0; c < pro; ++c) issue_chunk(c);
   }
 
-  bool failed = false;
+  bool failed = false, halo_landed = !halo_issued;
   if (clustered) {
     // Every CTA of the cluster holds its halo rows before any CTA stores: a split reads the
     // first rows of the next split before that split overwrites them.  Only loads precede
     // this barrier.
-    if (has_halo && !mbar_wait_bounded(halo_bar, 0)) failed = true;
+    if (halo_issued) {
+      halo_landed = mbar_wait_bounded(halo_bar, 0, polls);
+      if (!halo_landed) failed = true;
+    }
     cluster_sync();
   }
 
@@ -189,7 +200,12 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
 #pragma unroll 1
   for (int c = 0; c < nchunks; ++c) {
     const int stage = c % S;
-    if (!failed && !mbar_wait_bounded(bar0 + 8 * stage, (c / S) & 1)) failed = true;
+    if (!failed) {
+      if (mbar_wait_bounded(bar0 + 8 * stage, (c / S) & 1, polls))
+        consumed = c + 1;
+      else
+        failed = true;
+    }
     const int x = a + c * T, xe = imin(x + T, e);
     KT* sk = reinterpret_cast<KT*>(stages + stage * STAGE);
     VT* sv = reinterpret_cast<VT*>(stages + stage * STAGE + T * KROW);
@@ -228,7 +244,15 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
   if (tid == 0) bulk_wait<0>();
   failed = __syncthreads_or(failed);
   allow_dependents();
-  if (failed && tid == 0) atomicOr(A.status, 1);
+  if (failed && tid == 0) {
+    atomicOr(A.status, 1);
+    // Drain: every load issued but not seen to land (the chunk whose wait ran out included,
+    // unless it was never issued) gets one more bounded wait.  At most S - 1 chunks are in
+    // flight at a failure, on distinct stages, so each stage's phase is unambiguous.
+    for (int c = consumed; c < issued; ++c)
+      if (c != A.skip_chunk) mbar_wait_bounded(bar0 + 8 * (c % S), (c / S) & 1, polls);
+    if (!halo_landed) mbar_wait_bounded(halo_bar, 0, polls);
+  }
   // A clustered CTA stays for the cluster barriers below (its results are void).
   if (failed && !clustered) return;
 

@@ -1,8 +1,9 @@
 // Ring-buffer ("v2") cache step: the new token is written over one ring slot and the few
 // region keys (sinks, pinned tokens) are rotated from their stored originals to sit just
 // before the window (src/sinkcache/cache_v2.py:101-116 _rotate_region, :167-181
-// _decode_step).  Window keys are never touched; attention over ring + region is the
-// stream kernel in attend-only mode.
+// _decode_step).  Window keys are never touched; attention over ring + region runs on the
+// tensor-core kernel (sink_attend_tc_kernel) for 16-bit keys at head_dim 128, else on the
+// stream kernel in attend-only mode, then the split combine.
 #pragma once
 
 #include "sink_common.cuh"

@@ -321,8 +321,18 @@ constexpr int cluster_warps() {
   return 9 * GMAX * (D + 2) * 4 <= Gm::S * Gm::STAGE ? 8 : 4;
 }
 
+// Failure-detection test hook (sink_debug_fail_next_wait): armed as (chunk << 32) | polls,
+// consumed by the next stream-kernel launch of the process; -1 when disarmed.
+std::atomic<int64_t> g_fail_next_wait{-1};
+
 template <typename KT, typename VT, int D, int GMAX, bool ATTEND>
-int32_t launch_stream(const StreamArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev) {
+int32_t launch_stream(const StreamArgs& A0, const Plan& pl, int pairs, cudaStream_t st, int dev) {
+  StreamArgs A = A0;
+  const int64_t inject = g_fail_next_wait.exchange(-1, std::memory_order_acq_rel);
+  if (inject >= 0) {
+    A.skip_chunk = int(inject >> 32);
+    A.wait_polls = int(inject & 0x7fffffff);
+  }
   using Gm = StreamGeom<KT, VT, D>;
   if (Gm::SMEM != pl.smem || Gm::T != pl.T) return SINK_EINVAL;  // host/device geometry drift
   // clustered launches (one CTA per SM in the latency regime) run 8 warps per CTA where the
@@ -439,20 +449,28 @@ void fill_common(StreamArgs& A, const sink_kv_buffers_t* kv, const Plan& pl, cha
   A.halo_k = pl.off_hk ? ws + pl.off_hk : nullptr;
   A.halo_v = pl.off_hv ? ws + pl.off_hv : nullptr;
   A.cluster = pl.cluster ? 1 : 0;
+  A.wait_polls = kWaitPolls;
+  A.skip_chunk = -1;
 }
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Checks shared by the attention entry points, and the plan they launch with.
-int32_t plan_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows, void* out,
-                       void* workspace, size_t workspace_bytes, Plan& pl, int* dev) {
+// Argument checks shared by the attention entry points, and the plan they launch with
+// (everything but the workspace).
+int32_t plan_attention_args(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows, void* out,
+                            Plan& pl, int* dev) {
   if (!q || !q->data || !out) return SINK_EINVAL;
   if (q->dtype != kv->v_dtype) return SINK_EDTYPE;
   if (q->n != 1 || rows < 1 || rows > kv->slots) return SINK_EINVAL;
   const int sms = device_sms(dev);
   if (sms <= 0) return SINK_EDEVICE;
-  const int32_t rc = make_plan(SINK_OP_ATTEND, kv->batch, kv->heads_kv, q->heads, kv->head_dim,
-                               kv->k_dtype, kv->v_dtype, rows, 0, 1, 0, sms, pl);
+  return make_plan(SINK_OP_ATTEND, kv->batch, kv->heads_kv, q->heads, kv->head_dim, kv->k_dtype,
+                   kv->v_dtype, rows, 0, 1, 0, sms, pl);
+}
+
+int32_t plan_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows, void* out,
+                       void* workspace, size_t workspace_bytes, Plan& pl, int* dev) {
+  const int32_t rc = plan_attention_args(q, kv, rows, out, pl, dev);
   if (rc) return rc;
   if (!workspace || workspace_bytes < pl.total || !aligned16(workspace)) return SINK_EWORKSPACE;
   return SINK_OK;
@@ -748,6 +766,34 @@ int32_t launch_v2_place(const sink_kv_buffers_t* kv, const V2PlaceArgs& a, int s
 }
 
 
+// ---------------------------------------------------------------- no-allocation scratch
+
+}  // namespace
+
+// Scratch of sink_decode_attention_noalloc.  In host code this name is only a stand-in for
+// the symbol, not a device address: the host looks up each device's copy with
+// cudaGetSymbolAddress and passes that pointer to the kernels.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[SINK_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+// Device address of g_noalloc_scratch on device `dev` (the current device), looked up once
+// per device: by sink_prepare_device, or by the first no-allocation call on that device.
+int32_t noalloc_scratch(int dev, void** ptr) {
+  static std::atomic<void*> cache[64];
+  if (dev < 0 || dev >= 64) return SINK_EDEVICE;
+  void* p = cache[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess) return err;
+    if (p == nullptr) return SINK_EDEVICE;
+    cache[dev].store(p, std::memory_order_release);
+  }
+  *ptr = p;
+  return SINK_OK;
+}
+
+
 // ---------------------------------------------------------------- per-device set-up
 
 // Opt every kernel that uses more than 48 KB of dynamic shared memory into its size, and
@@ -849,6 +895,9 @@ int32_t prepare_device(int dev) {
   if (e != cudaSuccess) return e;
   tc_cluster_capacity(dev);
   if (tensor_map_encoder() == nullptr) return SINK_EDEVICE;
+  void* scratch = nullptr;  // the no-allocation entry point's static array, on this device
+  const int32_t rc = noalloc_scratch(dev, &scratch);
+  if (rc) return rc;
   g_prepared.fetch_or(bit, std::memory_order_acq_rel);
   return SINK_OK;
 }
@@ -1080,6 +1129,12 @@ int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_ne
                           out_stride_h, workspace, pl, dev, st);
 }
 
+int32_t sink_debug_fail_next_wait(int32_t chunk, int32_t polls) {
+  if (chunk < 0 || polls < 1) return SINK_EINVAL;
+  g_fail_next_wait.store((int64_t(chunk) << 32) | int64_t(polls), std::memory_order_release);
+  return SINK_OK;
+}
+
 int32_t sink_prepare_device(void) {
   int dev = 0;
   if (device_sms(&dev) <= 0) return SINK_EDEVICE;
@@ -1100,52 +1155,24 @@ int32_t sink_read_status(void* workspace, void* stream, int32_t* status) {
 
 }  // extern "C"
 
-// ------------------------------------------------------------------ no-allocation variant
-
-// Scratch of sink_decode_attention_noalloc.  In host code this name is only a stand-in for
-// the symbol, not a device address: the host looks up each device's copy with
-// cudaGetSymbolAddress and passes that pointer to the kernels.
-static __device__ __align__(256) unsigned char g_noalloc_scratch[SINK_NOALLOC_SCRATCH_BYTES];
-
-namespace {
-
-// Device address of g_noalloc_scratch on device `dev` (the current device), looked up once.
-int32_t noalloc_scratch(int dev, void** ptr) {
-  static std::atomic<void*> cache[64];
-  void* p = cache[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {
-    const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (err != cudaSuccess) return err;
-    if (p == nullptr) return SINK_EDEVICE;
-    cache[dev].store(p, std::memory_order_release);
-  }
-  *ptr = p;
-  return SINK_OK;
-}
-
-}  // namespace
-
 extern "C" int32_t sink_decode_attention_noalloc(const sink_rows_t* q, const sink_kv_buffers_t* kv,
                                                  int32_t rows, float scale, const uint8_t* mask,
                                                  int64_t mask_stride_b, void* out,
                                                  int64_t out_stride_b, int64_t out_stride_h,
                                                  void* stream) {
+  // Every argument check of sink_decode_attention runs first, so a bad request returns the
+  // same code as there and launches nothing; only then the scratch size.
   int32_t rc = check_kv(kv);
   if (rc) return rc;
-  if (!q || !q->data || !out) return SINK_EINVAL;
-  int dev = 0;
-  const int sms = device_sms(&dev);
-  if (sms <= 0) return SINK_EDEVICE;
   Plan pl;
-  rc = make_plan(SINK_OP_ATTEND, kv->batch, kv->heads_kv, q->heads, kv->head_dim, kv->k_dtype,
-                 kv->v_dtype, rows, 0, 1, 0, sms, pl);
-  if (rc) return rc;
+  int dev = 0;
+  if ((rc = plan_attention_args(q, kv, rows, out, pl, &dev))) return rc;
   if (pl.total > SINK_NOALLOC_SCRATCH_BYTES) return SINK_ESCRATCH;
   void* scratch = nullptr;
   if ((rc = noalloc_scratch(dev, &scratch))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const cudaError_t err = cudaMemsetAsync(scratch, 0, sizeof(int32_t), st);  // status word
   if (err != cudaSuccess) return err;
-  return sink_decode_attention(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
-                               out_stride_h, scratch, SINK_NOALLOC_SCRATCH_BYTES, stream);
+  return launch_attention(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b, out_stride_h,
+                          scratch, pl, dev, st);
 }

@@ -36,8 +36,27 @@ def flash_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float
     if v.shape[-2] > 1 and v.stride(-2) != dim:
         v = v.contiguous()
     out = torch.empty(bsz, 1, hq, dim, device=q.device, dtype=q.dtype)
-    ws = _lib.Workspace()  # per call, like the reference's partials: safe under graph capture
-    return _lib.decode_attention(q, k, v, k.shape[2], scale, out, ws, mask)
+    return _lib.decode_attention(q, k, v, k.shape[2], scale, out, _workspace_for(q.device), mask)
+
+
+# Workspaces of flash_decode, one per (device, stream): calls on one stream run in order, so
+# they can share one; a call on another stream gets its own.
+_WORKSPACES: dict[tuple[int, int], _lib.Workspace] = {}
+
+
+def _workspace_for(device: torch.device) -> _lib.Workspace:
+    """The workspace of this device's current stream, grown on demand and reused across
+    calls (no allocation or memset per call).  Inside a CUDA-graph capture a fresh one is
+    allocated from the graph's memory pool instead, as the reference allocates its
+    partials per call: a cached buffer grown during a capture would belong to that pool."""
+    if device.type != "cuda" or torch.cuda.is_current_stream_capturing():
+        return _lib.Workspace()
+    stream = torch.cuda.current_stream(device)
+    key = (stream.device_index, stream.cuda_stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None:
+        ws = _WORKSPACES[key] = _lib.Workspace()
+    return ws
 
 
 def _on_kernel_device(query: torch.Tensor) -> bool:

@@ -246,6 +246,21 @@ int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_ne
                             int64_t out_stride_b, int64_t out_stride_h, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/*
+ * Failure-detection test hook; no counterpart in the reference (which records only
+ * out-of-memory failures).  Arms the NEXT launch of the stream kernel in this process -- the
+ * kernel behind sink_evict_rerotate, sink_fused_decode_step, and sink_decode_attention over
+ * float32 keys or head_dim 64/256 -- so that every CTA leaves its row chunk `chunk` (0 = the
+ * first of its split) unissued: no copy and no arrival, so the wait for that chunk runs
+ * out after `polls` polls (each of that launch's waits is bounded by `polls`).  The CTAs then
+ * wait for the copies they did issue, store nothing further, and set
+ * SINK_STATUS_WAIT_TIMEOUT in the workspace status word; the context stays usable.  CTAs
+ * whose split has no chunk `chunk` run normally.  A launch that fails this way leaves an
+ * in-place eviction partly applied, so the caller restores the buffers (a read-only
+ * attention leaves them untouched).  Returns 0, or SINK_EINVAL for chunk < 0 or polls < 1.
+ */
+int32_t sink_debug_fail_next_wait(int32_t chunk, int32_t polls);
+
 /* Size of the static device scratch behind sink_decode_attention_noalloc: 16 MiB. */
 #define SINK_NOALLOC_SCRATCH_BYTES (16u << 20)
 
@@ -259,11 +274,13 @@ int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_ne
  * file-scope 16 MiB device array (SINK_NOALLOC_SCRATCH_BYTES) that every GPU which loads
  * the library holds until the process exits (on a B200 it holds, e.g., 16 streams of a
  * 32K-slot Qwen3 layer).
- *   - The first call on a device looks up that device's copy of the array
- *     (cudaGetSymbolAddress, with the device current); make that first call before any
- *     stream capture.
- *   - A request whose scratch (sink_workspace_bytes(SINK_OP_ATTEND, ...)) exceeds the array
- *     returns SINK_ESCRATCH and launches nothing.
+ *   - Each device's copy of the array is looked up once (cudaGetSymbolAddress, with the
+ *     device current) by sink_prepare_device(), or else by the first call on that device;
+ *     either must happen before any stream capture.
+ *   - The arguments are checked exactly as sink_decode_attention checks them (same error
+ *     codes, nothing launched); then a request whose scratch
+ *     (sink_workspace_bytes(SINK_OP_ATTEND, ...)) exceeds the array returns SINK_ESCRATCH
+ *     and launches nothing.
  *   - All calls share the one array and each call leaves its partials there: calls that can
  *     overlap on the GPU (different streams, different host threads) race and must be
  *     serialised by the caller.  Each call clears the array's status word first; the

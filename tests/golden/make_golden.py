@@ -1,7 +1,8 @@
 """Generate the golden fixtures by running the reference itself (buttaRahul/Attention_sinks,
 imported from its source tree) on the CPU.
 
-    python tests/golden/make_golden.py [--reference /root/reference/src] [--config1]
+    SINKCACHE_REFERENCE_SRC=<reference checkout>/src python tests/golden/make_golden.py [--config1 N]
+    python tests/golden/make_golden.py --reference <reference checkout>/src [--config1 N]
 
 Writes tests/golden/golden.json (known answers, digests) and tests/golden/arrays.npz
 (small output arrays).  The reference is pure Python; its PyTorch eviction path and the
@@ -279,10 +280,13 @@ def config1_case(ref, out, arrays, steps):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference/src")
+    ap.add_argument("--reference", default=os.environ.get("SINKCACHE_REFERENCE_SRC"),
+                    help="the reference's src/ directory (default: $SINKCACHE_REFERENCE_SRC)")
     ap.add_argument("--config1", type=int, default=0, help="also stream N steps of random-init Qwen3-0.6B")
     ap.add_argument("--only", default="", help="comma-separated case functions to regenerate (default: all)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give the reference's src/ directory with --reference or SINKCACHE_REFERENCE_SRC")
     ref = load_reference(args.reference)
     json_path = os.path.join(HERE, "golden.json")
     npz_path = os.path.join(HERE, "arrays.npz")
