@@ -320,6 +320,22 @@ class SinkCache(Cache):
         for a bulk copy that ran out) since the last check; synchronises the stream."""
         self.workspace.check()
 
+    # What a captured steady step depends on, and what a replay cannot advance (used by
+    # StreamRunner).  Positions are in-cache here: a steady step always sits at `capacity`.
+    absolute_positions = False
+
+    def graph_signature(self):
+        """The buffers and workspace the step's kernels were captured with."""
+        ws = self.workspace.buf
+        return (tuple((l._kbuf.data_ptr(), l._vbuf.data_ptr()) for l in self.layers),
+                None if ws is None else ws.data_ptr())
+
+    def note_replayed_step(self) -> None:
+        """Counters of one replayed steady step: one token seen, one evicted, per layer."""
+        for layer in self.layers:
+            layer.tokens_seen += 1
+            layer.tokens_evicted += 1
+
     @property
     def tokens_evicted(self) -> int:
         return self.layers[0].tokens_evicted

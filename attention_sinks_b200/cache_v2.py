@@ -1,26 +1,34 @@
 """Ring-buffer attention-sink cache ("v2"): the sinks move forward, the window stays put
-(src/sinkcache/cache_v2.py:1-50).
+(the algorithm of src/sinkcache/cache_v2.py:1-50).
 
-RoPE attention depends only on relative position, so instead of re-rotating every window
+RoPE attention depends only on relative position.  So instead of re-rotating every window
 key each step (v1), window keys keep the rotation the model gave them at their absolute
-positions, the query sits at its absolute position t, and only the few region tokens (the
-sinks, plus pinned tokens) are rotated -- from stored originals, with fp64 angles -- to sit
-just before the window.  Keys are stored in the model dtype (no drift: window keys are never
-rounded again).
+positions, the query sits at its absolute position t, and only the few *region* tokens --
+the sinks, plus pinned tokens that have left the window -- are rotated, from their stored
+original keys and with fp64 angles, to sit just before the window.  Keys are stored in the
+model dtype: a window key is never rounded again.
 
-Storage per layer: a ring of window + 1 slots (position p >= n_sink in slot
-(p - n_sink) mod (window + 1)) followed by the region slots; attention reads one contiguous
-view, ring then region.
+Layout of one layer (what the kernels read): K and V buffers of `ring + region_cap` rows,
+ring = window + 1.  The token at absolute position p >= n_sink lives in ring slot
+(p - n_sink) mod ring; the region's rows follow the ring (rotated keys in K, values in V),
+in region order: sinks first, then pinned tokens in the order they left the window.  The
+region's original keys sit in a separate buffer with their positions on the device.
 
-Device work goes through the sm_100a library:
-  * steady one-token step: sink_v2_place (ring write + region rotation + device position
-    advance) and, when the model uses the registered attention backend, the same step fused
-    with split-K decode attention (sink_v2_decode_step);
-  * the region rotation of chunk steps and kept(): sink_v2_place into a gathered tensor.
-The general (chunk) step's gather of the window in position order and its stores are
-device tensor copies, as in the reference.  A steady step reads t from a device tensor,
-so one captured CUDA graph serves every later token (StreamRunner).
+Host state is small: the next position `t`, the region's positions, how far pins have been
+looked for (`moved_upto`) and how many the pin budget dropped.  The device keeps the
+position too ({t, arrival counter}), read and advanced by the steady-step kernel, so one
+captured CUDA graph serves every later steady token.
+
+Device work goes through the sm_100a library: the steady one-token step is sink_v2_place
+(or, when the model uses the registered attention backend, sink_v2_decode_step: the same
+step fused with its attention); chunk steps and kept() rotate the region with
+sink_v2_place into a fresh tensor and copy the window out of the ring as at most two
+contiguous slices per tensor.
 """
+
+from __future__ import annotations
+
+from dataclasses import dataclass
 
 import torch
 from transformers.cache_utils import Cache, CacheLayerMixin
@@ -29,8 +37,80 @@ from . import _lib
 from .cache import _BY_BUFFER, find_inv_freq, uses_sink_attention
 
 
+def _pins_between(pinned, lo: int, hi: int) -> list[int]:
+    """Pinned positions p with lo <= p < hi, ascending.  Probes the range when it is shorter
+    than the pin set (a steady step asks about one position), else filters the set."""
+    if hi <= lo or not pinned:
+        return []
+    if hi - lo <= len(pinned):
+        return [p for p in range(lo, hi) if p in pinned]
+    return sorted(p for p in pinned if lo <= p < hi)
+
+
+class _Region:
+    """The rows placed just before the window.
+
+    Entry j has an original key (`keys[:, :, j]`, at the rotation of its own position
+    `positions[j]`, mirrored on the device in `pos_dev[j]`) and a value (`values[:, :, j]`,
+    a view into the layer's V buffer right after the ring, where attention reads it).
+    Entries 0..n_sink-1 are the sinks; after them come pins.  When the region is full, a
+    new pin pushes out the oldest pin (entry n_sink) and the pins after it move up a row;
+    with no pin budget a full region is an error."""
+
+    def __init__(self, n_sink: int, max_pinned: int):
+        self.n_sink, self.max_pinned = n_sink, max_pinned
+        self.capacity = n_sink + max_pinned
+        self.positions: list[int] = []
+        self.dropped = 0
+        self.keys = self.values = self.pos_dev = None
+
+    def bind(self, keys: torch.Tensor, values: torch.Tensor, pos_dev: torch.Tensor) -> None:
+        self.keys, self.values, self.pos_dev = keys, values, pos_dev
+
+    def __len__(self) -> int:
+        return len(self.positions)
+
+    def add(self, k_row: torch.Tensor, v_row: torch.Tensor, position: int) -> None:
+        """k_row, v_row: [b, h, 1, d]; the key at the rotation of `position`."""
+        if len(self.positions) >= self.capacity:
+            if self.max_pinned == 0:
+                raise RuntimeError("region full")
+            self._drop_oldest_pin()
+        j = len(self.positions)
+        self.keys[:, :, j:j + 1].copy_(k_row)
+        self.values[:, :, j:j + 1].copy_(v_row)
+        self.pos_dev[j] = position
+        self.positions.append(position)
+
+    def _drop_oldest_pin(self) -> None:
+        first, n = self.n_sink, len(self.positions)
+        for rows in (self.keys, self.values, self.pos_dev.view(1, 1, -1, 1)):
+            rows[:, :, first:n - 1] = rows[:, :, first + 1:n].clone()  # overlapping move: copy first
+        del self.positions[first]
+        self.dropped += 1
+
+
+@dataclass
+class _LayerState:
+    """Everything restore() writes back into a layer (device copies plus host counters)."""
+    k: torch.Tensor
+    v: torch.Tensor
+    region_keys: torch.Tensor
+    region_pos: torch.Tensor
+    t: int
+    positions: list[int]
+    moved_upto: int
+
+
+@dataclass
+class V2Snapshot:
+    """SinkCacheV2.snapshot(): per-layer states and the pinned positions."""
+    layers: list[_LayerState]
+    pinned: frozenset
+
+
 class SinkLayerV2(CacheLayerMixin):
-    """One layer of the ring-buffer cache (src/sinkcache/cache_v2.py:59-248)."""
+    """One layer of the ring-buffer cache (the interface of src/sinkcache/cache_v2.py:59-248)."""
 
     is_sliding = False
     is_croppable = False
@@ -45,15 +125,23 @@ class SinkLayerV2(CacheLayerMixin):
         self.ring = window + 1
         self.region_cap = n_sink + max_pinned
         self.inv_freq = inv_freq
-        self.pinned = pinned if pinned is not None else set()
-        self.t = 0                       # absolute position of the next token = tokens seen
-        self.region_pos: list[int] = []  # original positions of region tokens (sinks, then pinned)
-        self.moved_upto = 0              # pinned positions below this have been handled
-        self.pins_dropped = 0
+        self.pinned = pinned if pinned is not None else set()  # shared with the cache's pin()
+        self.t = 0               # absolute position of the next token (= tokens seen)
+        self.moved_upto = 0      # pins below this position have been looked for
         self.fused = fused
+        self._region = _Region(n_sink, max_pinned)
         self._kbuf = self._vbuf = None
-        self._pending = None             # (k, v, R) of a deferred steady step
+        self._pending = None     # (k, v, region size) of a deferred steady step
         self._ws = workspace if workspace is not None else _lib.Workspace()
+
+    @property
+    def region_pos(self) -> list[int]:
+        """Original positions of the region entries (sinks, then pins)."""
+        return self._region.positions
+
+    @property
+    def pins_dropped(self) -> int:
+        return self._region.dropped
 
     # ------------------------------------------------------------------ storage
 
@@ -64,12 +152,14 @@ class SinkLayerV2(CacheLayerMixin):
         b, h, _, d = key_states.shape
         if 2 * self.inv_freq.numel() > d:
             raise ValueError(f"rotary dims {2 * self.inv_freq.numel()} exceed head_dim {d}")
-        n = self.ring + self.region_cap
-        self._kbuf = torch.zeros(b, h, n, d, dtype=self.dtype, device=self.device)
-        self._vbuf = torch.zeros(b, h, n, d, dtype=self.dtype, device=self.device)
-        self._reg_k = torch.zeros(b, h, max(self.region_cap, 1), d, dtype=self.dtype, device=self.device)
-        self._reg_pos = torch.zeros(max(self.region_cap, 1), dtype=torch.long, device=self.device)
-        # {t, arrival counter}: t is read and advanced by the steady-step kernel
+        rows = self.ring + self.region_cap
+        self._kbuf = torch.zeros(b, h, rows, d, dtype=self.dtype, device=self.device)
+        self._vbuf = torch.zeros(b, h, rows, d, dtype=self.dtype, device=self.device)
+        cap = max(self.region_cap, 1)
+        self._reg_k = torch.zeros(b, h, cap, d, dtype=self.dtype, device=self.device)
+        self._reg_pos = torch.zeros(cap, dtype=torch.long, device=self.device)
+        self._region.bind(self._reg_k, self._vbuf[:, :, self.ring:], self._reg_pos)
+        # {t, arrival counter}: the steady-step kernel reads t and advances it
         self._position = torch.zeros(2, dtype=torch.long, device=self.device)
         self._t_dev = self._position[0]
         self.inv_freq = self.inv_freq.to(self.device, torch.float64).contiguous()
@@ -88,98 +178,81 @@ class SinkLayerV2(CacheLayerMixin):
                                                   self.ring + R, 0, 1, 0, sms))
         self._ws.get(need, self.device)
 
-    def _slot(self, p: int) -> int:
-        return (p - self.n_sink) % self.ring
-
-    def _slots(self, lo: int, hi: int) -> torch.Tensor:
-        """Ring slots of positions [lo, hi) (all >= n_sink) as a device index tensor, computed
-        on the device (cache_v2.py:190, 202 build them as host lists)."""
-        return (torch.arange(lo, max(lo, hi), device=self.device) - self.n_sink) % self.ring
+    # ------------------------------------------------------------------ positions
 
     def _window_start(self, t: int) -> int:
+        """First window position when the next token is t (positions below n_sink count as
+        sinks, not window)."""
         return max(min(t, self.n_sink), t - self.window)
 
-    def _assemble(self, R: int, window: list[torch.Tensor], chunk: torch.Tensor | None,
-                  region: torch.Tensor | None = None) -> torch.Tensor:
-        """[region (R rows), window rows, chunk] in one new tensor, filled by slice copies
-        (torch.cat of these strided views runs far below the copy bandwidth).  Region rows
-        are copied from `region`, or left for the caller to write when it is None."""
-        b, h, _, d = self._kbuf.shape
-        n = R + sum(x.shape[-2] for x in window) + (chunk.shape[-2] if chunk is not None else 0)
-        out = torch.empty(b, h, n, d, dtype=self.dtype, device=self.device)
-        if region is not None and R:
-            out[:, :, :R].copy_(region)
-        o = R
-        for x in window + ([chunk] if chunk is not None else []):
-            out[:, :, o:o + x.shape[-2]].copy_(x)
-            o += x.shape[-2]
-        return out
+    def _window_span(self, t: int) -> tuple[int, int]:
+        """Window positions [lo, hi) held in the ring when the next token is t (empty while
+        t <= n_sink)."""
+        return max(self._window_start(t), self.n_sink), t
 
-    def _ring_rows(self, buf: torch.Tensor, lo: int, hi: int) -> list[torch.Tensor]:
-        """Rows of positions [lo, hi) (all >= n_sink, fewer than a ring) in position order, as
-        at most two contiguous views of the ring: the same rows the reference gathers with an
-        index list (cache_v2.py:189-193), without the gather."""
+    def _ring_views(self, buf: torch.Tensor, lo: int, hi: int) -> list[torch.Tensor]:
+        """Ring rows of positions [lo, hi) (all >= n_sink, at most a ring's worth) in position
+        order: one contiguous view, or two when the span wraps around the ring's end."""
         n = hi - lo
         if n <= 0:
             return []
-        s0 = (lo - self.n_sink) % self.ring
-        if s0 + n <= self.ring:
-            return [buf[:, :, s0:s0 + n]]
-        return [buf[:, :, s0:self.ring], buf[:, :, :s0 + n - self.ring]]
+        s = (lo - self.n_sink) % self.ring
+        head = min(n, self.ring - s)
+        views = [buf[:, :, s:s + head]]
+        if head < n:
+            views.append(buf[:, :, :n - head])
+        return views
 
-    # ------------------------------------------------------------------ rotation
-
-    def _rotate_region(self, t: int, out: torch.Tensor | None = None) -> torch.Tensor:
-        """Region keys rotated from their originals to positions ws-R..ws-1, ws the window
-        start when the next token is t (cache_v2.py:101-116), by the place kernel."""
-        R = len(self.region_pos)
+    def _stack_rows(self, n_region: int, parts: list[torch.Tensor],
+                    region: torch.Tensor | None) -> torch.Tensor:
+        """A new [b, h, n_region + rows of parts, d] tensor: region rows (copied from `region`,
+        or left for the caller), then the parts in order."""
         b, h, _, d = self._kbuf.shape
-        if out is None:
-            out = torch.empty(b, h, R, d, dtype=self.dtype, device=self.device)
-        if R:
-            _lib.v2_place(self._kbuf, self._vbuf, None, None, self._reg_k, self._reg_pos, R, out, None, t,
-                          self.n_sink, self.window, self.inv_freq)
+        total = n_region + sum(p.shape[-2] for p in parts)
+        out = torch.empty(b, h, total, d, dtype=self.dtype, device=self.device)
+        if region is not None and n_region:
+            out[:, :, :n_region].copy_(region)
+        at = n_region
+        for p in parts:
+            out[:, :, at:at + p.shape[-2]].copy_(p)
+            at += p.shape[-2]
         return out
 
-    # ------------------------------------------------------------------ region bookkeeping
+    def _logical(self, t: int, chunk: tuple[torch.Tensor, torch.Tensor] | None = None):
+        """(keys, values) of [region rotated to sit before the window, window by position,
+        chunk] for a query at position t."""
+        R = len(self._region)
+        lo, hi = self._window_span(t)
+        kparts = self._ring_views(self._kbuf, lo, hi) + ([chunk[0]] if chunk is not None else [])
+        vparts = self._ring_views(self._vbuf, lo, hi) + ([chunk[1]] if chunk is not None else [])
+        keys = self._stack_rows(R, kparts, None)
+        if R:  # the region's keys, rotated straight into the new tensor's first rows
+            _lib.v2_place(self._kbuf, self._vbuf, None, None, self._reg_k, self._reg_pos, R, keys[:, :, :R], None,
+                          t, self.n_sink, self.window, self.inv_freq)
+        values = self._stack_rows(R, vparts, self._region.values[:, :, :R])
+        return keys, values
 
-    def _region_append(self, k: torch.Tensor, v: torch.Tensor, p: int):
-        """k, v: [b, h, 1, d]; k at its original rotation (position p) (cache_v2.py:120-130)."""
-        if len(self.region_pos) == self.region_cap:
-            if self.max_pinned == 0:
-                raise RuntimeError("region full")
-            self._region_drop_oldest_pin()
-        j = len(self.region_pos)
-        self._reg_k[:, :, j:j + 1].copy_(k)
-        self._vbuf[:, :, self.ring + j:self.ring + j + 1].copy_(v)
-        self._reg_pos[j] = p
-        self.region_pos.append(p)
-
-    def _region_drop_oldest_pin(self):
-        """cache_v2.py:132-138"""
-        s, R, r = self.n_sink, len(self.region_pos), self.ring
-        self._reg_k[:, :, s:R - 1] = self._reg_k[:, :, s + 1:R].clone()
-        self._vbuf[:, :, r + s:r + R - 1] = self._vbuf[:, :, r + s + 1:r + R].clone()
-        self._reg_pos[s:R - 1] = self._reg_pos[s + 1:R].clone()
-        del self.region_pos[s]
-        self.pins_dropped += 1
-
-    def _move_pins(self, bound: int, chunk=None):
-        """Pinned positions in [moved_upto, bound) have left the window: into the region
-        (cache_v2.py:140-151)."""
-        if self.pinned and bound > self.moved_upto:
-            for p in sorted(p for p in self.pinned if self.moved_upto <= p < bound and p >= self.n_sink):
-                if chunk is not None and p >= chunk[2]:
-                    i = p - chunk[2]
-                    self._region_append(chunk[0][:, :, i:i + 1], chunk[1][:, :, i:i + 1], p)
-                else:
-                    sl = self._slot(p)
-                    self._region_append(self._kbuf[:, :, sl:sl + 1], self._vbuf[:, :, sl:sl + 1], p)
-        self.moved_upto = max(self.moved_upto, bound)
+    # ------------------------------------------------------------------ pins
 
     def next_step_moves_pin(self) -> bool:
-        """Would a one-token step at the current position move a pin afterwards?"""
-        return (self.t - self.window) in self.pinned and self.t - self.window >= self.n_sink
+        """Would a one-token step at the current position move a pin into the region?"""
+        p = self.t - self.window
+        return p >= self.n_sink and p in self.pinned
+
+    def _pins_leave(self, bound: int, chunk=None) -> None:
+        """Pins below `bound` have left the window: each joins the region, its rows taken
+        from its ring slot or, for a position of the chunk being stored (chunk = (k, v,
+        first position)), from the chunk."""
+        if bound <= self.moved_upto:
+            return
+        for p in _pins_between(self.pinned, max(self.moved_upto, self.n_sink), bound):
+            if chunk is not None and p >= chunk[2]:
+                i = p - chunk[2]
+                self._region.add(chunk[0][:, :, i:i + 1], chunk[1][:, :, i:i + 1], p)
+            else:
+                s = (p - self.n_sink) % self.ring
+                self._region.add(self._kbuf[:, :, s:s + 1], self._vbuf[:, :, s:s + 1], p)
+        self.moved_upto = bound
 
     # ------------------------------------------------------------------ cache API
 
@@ -187,25 +260,25 @@ class SinkLayerV2(CacheLayerMixin):
         if not self.is_initialized:
             self.lazy_initialization(key_states, value_states)
         self.materialize()
-        q = key_states.shape[-2]
-        if q == 1 and self.t >= self.n_sink + self.window:
-            return self._decode_step(key_states, value_states)
-        return self._general_step(key_states, value_states)
+        if key_states.shape[-2] == 1 and self.t >= self.n_sink + self.window:
+            return self._steady_step(key_states, value_states)
+        return self._chunk_step(key_states, value_states)
 
-    def _decode_step(self, k, v):
-        """Steady state (cache_v2.py:167-181): device-side slot and position only, so the step
-        can be captured in a CUDA graph.  Fused mode defers the place kernel to the attention
-        backend, unless this step moves a pin (then the region changes before attention
-        runs, exactly as in the reference, so the step is placed now)."""
-        R = len(self.region_pos)
+    def _steady_step(self, k, v):
+        """A one-token step on a full window: the token overwrites the ring slot of the one
+        that left the window last step, and the region is re-placed before the new window --
+        device-side slot and position only, so the step can be captured in a CUDA graph.
+        Fused mode leaves the kernel to the attention backend, unless this step moves a pin
+        (the region then changes before attention runs, so the step is placed now)."""
+        R = len(self._region)
         if self.fused and not self.next_step_moves_pin():
             self._pending = (k, v, R)
         else:
             self._place(k, v, R)
         self.t += 1
-        self._move_pins(self.t - self.window)
-        n = self.ring + R
-        self.keys, self.values = self._kbuf[:, :, :n], self._vbuf[:, :, :n]
+        self._pins_leave(self.t - self.window)
+        rows = self.ring + R
+        self.keys, self.values = self._kbuf[:, :, :rows], self._vbuf[:, :, :rows]
         return self.keys, self.values
 
     def _place(self, k, v, R):
@@ -223,47 +296,43 @@ class SinkLayerV2(CacheLayerMixin):
 
     def materialize(self) -> None:
         """Apply a deferred step without its attention."""
-        if self._pending is None:
-            return
-        k, v, R = self._pending
-        self._pending = None
-        self._place(k, v, R)
+        if self._pending is not None:
+            k, v, R = self._pending
+            self._pending = None
+            self._place(k, v, R)
 
-    def _general_step(self, k, v):
-        """Any chunk, warm-up, or a one-token step before the window is full
-        (cache_v2.py:183-208): attention gets [region (rotated), window in position order,
-        new chunk]; then the new tokens are stored."""
-        t, q = self.t, k.shape[-2]
-        ws = self._window_start(t)
-        R = len(self.region_pos)
-        lo = max(ws, self.n_sink)
-        r = self.ring
-        keys = self._assemble(R, self._ring_rows(self._kbuf, lo, t), k)
-        self._rotate_region(t, keys[:, :, :R])
-        values = self._assemble(R, self._ring_rows(self._vbuf, lo, t), v, self._vbuf[:, :, r:r + R])
-
-        for i in range(q):
-            if t + i < self.n_sink:
-                self._region_append(k[:, :, i:i + 1], v[:, :, i:i + 1], t + i)
-        self._move_pins(t + q - self.window, chunk=(k, v, t))
-        lo = max(self.n_sink, t + q - self.ring, t)
-        if lo < t + q:
-            idx = self._slots(lo, t + q)
-            self._kbuf.index_copy_(2, idx, k[:, :, lo - t:])
-            self._vbuf.index_copy_(2, idx, v[:, :, lo - t:])
-        self.t = t + q
-        self._t_dev.fill_(self.t)
+    def _chunk_step(self, k, v):
+        """Any chunk, the warm-up, or a one-token step before the window is full: attention
+        gets a fresh [region, window, chunk] tensor; then the chunk is stored -- positions
+        below n_sink join the region, pins that the chunk pushes out of the window join it
+        next, and the chunk's positions that stay within a ring's reach go to their slots."""
+        t, n = self.t, k.shape[-2]
+        keys, values = self._logical(t, (k, v))
+        end = t + n
+        for p in range(t, min(end, self.n_sink)):
+            self._region.add(k[:, :, p - t:p - t + 1], v[:, :, p - t:p - t + 1], p)
+        self._pins_leave(end - self.window, chunk=(k, v, t))
+        first = max(self.n_sink, end - self.ring, t)
+        if first < end:
+            done = first - t
+            for buf, src in ((self._kbuf, k), (self._vbuf, v)):
+                at = done
+                for view in self._ring_views(buf, first, end):
+                    view.copy_(src[:, :, at:at + view.shape[-2]])
+                    at += view.shape[-2]
+        self.t = end
+        self._t_dev.fill_(end)
         self.keys, self.values = keys, values
         return keys, values
 
     def get_seq_length(self) -> int:
-        """Absolute position of the next token (Transformers builds position_ids from this)."""
+        """Absolute position of the next token (Transformers builds position_ids from it)."""
         return self.t
 
     def in_cache_length(self) -> int:
-        """Tokens a new query attends to besides itself: region + current window."""
-        return len(self.region_pos) + (self.t - max(self._window_start(self.t), self.n_sink)
-                                       if self.t > self.n_sink else 0)
+        """Rows a new query attends to besides itself: region + current window."""
+        lo, hi = self._window_span(self.t)
+        return len(self._region) + max(0, hi - lo)
 
     def get_mask_sizes(self, query_length: int) -> tuple[int, int]:
         """(kv_length, kv_offset) of the attention mask over [region, window, chunk].
@@ -281,23 +350,19 @@ class SinkLayerV2(CacheLayerMixin):
         return self.region_cap + self.window
 
     def kept(self) -> tuple[torch.Tensor, torch.Tensor, list[int]]:
-        """Logical cache for the next query: keys/values in order [region, window by
-        position], and the positions they are rotated at (cache_v2.py:225-236)."""
+        """The logical cache for the next query: keys and values in the order [region,
+        window by position], and the position each key is rotated at (region entries just
+        before the window, window tokens at their own)."""
         self.materialize()
         t = self.t
-        ws = self._window_start(t)
-        R = len(self.region_pos)
-        win = list(range(max(ws, self.n_sink), t))
-        r = self.ring
-        lo = win[0] if win else t
-        k = self._assemble(R, self._ring_rows(self._kbuf, lo, t), None)
-        self._rotate_region(t, k[:, :, :R])
-        v = self._assemble(R, self._ring_rows(self._vbuf, lo, t), None, self._vbuf[:, :, r:r + R])
-        return k, v, [ws - R + j for j in range(R)] + win
+        keys, values = self._logical(t)
+        lo, hi = self._window_span(t)
+        R, ws = len(self._region), self._window_start(t)
+        return keys, values, list(range(ws - R, ws)) + list(range(lo, hi))
 
     def reset(self) -> None:
-        self.t = self.moved_upto = self.pins_dropped = 0
-        self.region_pos = []
+        self.t = self.moved_upto = 0
+        self._region = _Region(self.n_sink, self.max_pinned)
         self.keys = self.values = None
         self._pending = None
         self.is_initialized = False
@@ -308,10 +373,28 @@ class SinkLayerV2(CacheLayerMixin):
     def reorder_cache(self, beam_idx):
         raise NotImplementedError("beam search is not supported")
 
+    # ------------------------------------------------------------------ snapshots
+
+    def _state(self) -> _LayerState:
+        self.materialize()
+        return _LayerState(self._kbuf.clone(), self._vbuf.clone(), self._reg_k.clone(), self._reg_pos.clone(),
+                           self.t, list(self._region.positions), self.moved_upto)
+
+    def _load(self, s: _LayerState) -> None:
+        """Write a saved state back into the same buffers (pointers kept, so a captured graph
+        stays valid)."""
+        self._pending = None
+        for dst, src in ((self._kbuf, s.k), (self._vbuf, s.v), (self._reg_k, s.region_keys),
+                         (self._reg_pos, s.region_pos)):
+            dst.copy_(src)
+        self.t, self.moved_upto = s.t, s.moved_upto
+        self._region.positions[:] = s.positions
+        self._position.copy_(torch.tensor([s.t, 0], dtype=torch.long))
+
 
 class SinkCacheV2(Cache):
-    """Attention sinks with the sinks moved forward and the window left alone
-    (src/sinkcache/cache_v2.py:251-328).
+    """Attention sinks with the sinks moved forward and the window left alone (the interface
+    of src/sinkcache/cache_v2.py:251-328).
 
         cache = SinkCacheV2.from_model(model, n_sink=4, window=1020)
         out = model(input_ids, past_key_values=cache, use_cache=True)
@@ -321,21 +404,24 @@ class SinkCacheV2(Cache):
     one-token steps fused with their attention.
     """
 
+    # position ids of a steady step come from the stream start, not from the buffer: a
+    # graph-replayed step needs them fed from a device tensor (StreamRunner)
+    absolute_positions = True
+
     def __init__(self, n_sink: int, window: int, inv_freq: torch.Tensor, num_layers: int, max_pinned: int = 0,
                  fused: bool = False):
-        self.pinned: set[int] = set()
+        self.pinned: set[int] = set()  # one set for every layer
         self.workspace = _lib.Workspace()  # one for all layers: they run in order on one stream
-        layers = [SinkLayerV2(n_sink, window, inv_freq, max_pinned, self.pinned, fused=fused,
-                              workspace=self.workspace) for _ in range(num_layers)]
-        super().__init__(layers=layers)
+        super().__init__(layers=[SinkLayerV2(n_sink, window, inv_freq, max_pinned, self.pinned, fused=fused,
+                                             workspace=self.workspace) for _ in range(num_layers)])
         self.n_sink, self.window, self.max_pinned = n_sink, window, max_pinned
 
     @classmethod
     def from_model(cls, model, n_sink: int = 4, window: int = 1020, **kwargs) -> "SinkCacheV2":
         config = model.config.get_text_config(decoder=True)
-        layer_types = getattr(config, "layer_types", None) or ["full_attention"] * config.num_hidden_layers
-        if any(t != "full_attention" for t in layer_types):
-            raise ValueError(f"SinkCacheV2 supports full-attention models only, got {set(layer_types)}")
+        kinds = set(getattr(config, "layer_types", None) or ["full_attention"])
+        if kinds != {"full_attention"}:
+            raise ValueError(f"SinkCacheV2 supports full-attention models only, got {kinds}")
         kwargs.setdefault("fused", uses_sink_attention(model))
         return cls(n_sink, window, find_inv_freq(model), config.num_hidden_layers, **kwargs)
 
@@ -343,11 +429,13 @@ class SinkCacheV2(Cache):
         return self.layers[layer_idx].in_cache_length()
 
     def pin(self, start: int, end: int) -> None:
-        """Pin absolute positions [start, end).  Must be called before they leave the window."""
+        """Keep absolute positions [start, end) when they leave the window (they move into
+        the region).  Positions already past the window cannot be pinned."""
         if self.max_pinned == 0:
             raise ValueError("cache was built with max_pinned=0")
-        if start < self.layers[0].moved_upto:
-            raise ValueError(f"positions before {self.layers[0].moved_upto} have already been evicted")
+        gone = self.layers[0].moved_upto
+        if start < gone:
+            raise ValueError(f"positions before {gone} have already been evicted")
         self.pinned.update(range(start, end))
 
     @property
@@ -356,8 +444,8 @@ class SinkCacheV2(Cache):
 
     @property
     def tokens_evicted(self) -> int:
-        layer = self.layers[0]
-        return layer.t - layer.in_cache_length()
+        first = self.layers[0]
+        return first.t - first.in_cache_length()
 
     @property
     def region_size(self) -> int:
@@ -365,37 +453,46 @@ class SinkCacheV2(Cache):
 
     @property
     def is_steady(self) -> bool:
-        """The next one-token step takes the device-only path and moves no pin: safe to
-        capture/replay."""
-        layer = self.layers[0]
-        return (layer.is_initialized and layer.t >= self.n_sink + self.window
-                and not layer.next_step_moves_pin())
+        """The next one-token step is the device-only steady step and moves no pin: it can
+        be captured once and replayed."""
+        first = self.layers[0]
+        return (first.is_initialized and first.t >= self.n_sink + self.window
+                and not first.next_step_moves_pin())
 
-    def layout_key(self):
-        """What changes the captured computation: the region size (attention length)."""
-        return self.region_size
+    def check_status(self) -> None:
+        """Raise RuntimeError if one of this cache's kernels reported a failure since the
+        last check; synchronises the stream."""
+        self.workspace.check()
 
-    def advance_after_replay(self):
+    # what a captured steady step depends on, and what a replay cannot advance
+
+    def graph_signature(self):
+        """Buffers and workspace the kernels were captured with, and the region size (the
+        attention length)."""
+        ws = self.workspace.buf
+        return (tuple((l._kbuf.data_ptr(), l._vbuf.data_ptr()) for l in self.layers),
+                None if ws is None else ws.data_ptr(), self.region_size)
+
+    def note_replayed_step(self) -> None:
+        """Host counters of one replayed steady step (the device position advanced itself)."""
         for layer in self.layers:
             layer.t += 1
             layer.moved_upto = max(layer.moved_upto, layer.t - layer.window)
 
-    def snapshot(self):
-        """Device copies of all state; restore() writes them back in place (buffer pointers
-        kept, so a captured CUDA graph stays valid) (cache_v2.py:315-319)."""
-        for layer in self.layers:
-            layer.materialize()
-        return [(l._kbuf.clone(), l._vbuf.clone(), l._reg_k.clone(), l._reg_pos.clone(), l.t,
-                 list(l.region_pos), l.moved_upto) for l in self.layers], set(self.pinned)
+    # the reference's names for the two (src/sinkcache/cache_v2.py:302-313)
+    def layout_key(self):
+        return self.region_size
 
-    def restore(self, snap):
-        """cache_v2.py:321-328"""
-        layers, pinned = snap
-        for l, (kb, vb, rk, rp, t, rpos, mu) in zip(self.layers, layers):
-            l._pending = None
-            l._kbuf.copy_(kb), l._vbuf.copy_(vb), l._reg_k.copy_(rk), l._reg_pos.copy_(rp)
-            l.t, l.region_pos, l.moved_upto = t, list(rpos), mu
-            l._position.zero_()
-            l._t_dev.fill_(t)
+    def advance_after_replay(self) -> None:
+        self.note_replayed_step()
+
+    def snapshot(self) -> V2Snapshot:
+        """Device copies of every layer's state and the pinned positions; restore() writes
+        them back in place (buffer pointers kept, so a captured CUDA graph stays valid)."""
+        return V2Snapshot([layer._state() for layer in self.layers], frozenset(self.pinned))
+
+    def restore(self, snap: V2Snapshot) -> None:
+        for layer, state in zip(self.layers, snap.layers, strict=True):
+            layer._load(state)
         self.pinned.clear()
-        self.pinned.update(pinned)
+        self.pinned.update(snap.pinned)

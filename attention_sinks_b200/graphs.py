@@ -1,91 +1,115 @@
-"""One-token streaming with a CUDA graph for the steady state (src/sinkcache/graphs.py:1-86).
+"""Steady-state streaming through one captured CUDA graph per cache layout.
 
-SinkCache (v1): once full, every decode step is the same computation -- same shapes, same
-position (n_sink + window), same buffers, drop == 1.  One captured step (every kernel of
-the model forward including the sink-cache kernels, which take no host-side decisions
-inside a step) is replayed for every later token.
+Contract kept from the reference's StreamRunner (src/sinkcache/graphs.py:28-86): `step(ids)`
+returns the logits of a [batch, q] token step; a one-token step on a steady cache is replayed
+from a captured graph, everything else runs the model eagerly; a change of the cache's
+layout (reallocated buffers, a different attention length) makes the next steady step
+capture again; the cache's host-side counters, which no replay can move, are advanced after
+each replay.
 
-SinkCacheV2: shapes and buffers are fixed too, but the position grows.  The ring slot and
-the region rotation come from a device-side position inside each layer (read and advanced
-by the place kernel), and position_ids are fed from a static device tensor, so one captured
-step still serves every later token.  A step that moves a pinned token into the region
-runs eagerly, and a change of region size (attention length) triggers a recapture.
+How it is built here.  The cache itself answers the three questions a replay depends on:
+`is_steady` (is every further one-token step the same kernel sequence?),
+`graph_signature()` (the pointers and sizes a captured step has baked in) and
+`note_replayed_step()` (advance the counters a replay did not run).  A cache that counts
+positions from the start of the stream rather than inside its buffer (SinkCacheV2:
+`absolute_positions`) also gets the step's position ids from a static device tensor that is
+refilled before each replay.  Every kernel of the sink-cache path takes its decisions on the
+host before the step or reads them from device memory, so the graph never goes stale inside
+one layout.
 
-Python-side counters do not advance inside a replay, so the runner advances them.
+Each runner keeps at most one captured step (a layout change frees the old one) and warms
+the model up once on a side stream before its first capture, so that libraries the model
+calls finish their lazy set-up outside the capture.
 """
+
+from __future__ import annotations
 
 import torch
 
-from .cache import SinkCache
-from .cache_v2 import SinkCacheV2
+
+class _CapturedStep:
+    """One captured one-token step: the graph, the static tensors it reads (token ids,
+    position ids) and writes (logits), and the cache layout it was captured against."""
+
+    __slots__ = ("graph", "ids", "positions", "logits", "signature")
+
+    def __init__(self, signature, ids: torch.Tensor, positions: torch.Tensor | None):
+        self.graph = torch.cuda.CUDAGraph()
+        self.signature = signature
+        self.ids = ids
+        self.positions = positions
+        self.logits = None
+
+    def run(self, ids: torch.Tensor, position: int) -> torch.Tensor:
+        self.ids.copy_(ids)
+        if self.positions is not None:
+            self.positions.fill_(position)
+        self.graph.replay()
+        return self.logits
 
 
 class StreamRunner:
+    """Feeds a model token steps over a sink cache, replaying steady one-token steps from a
+    CUDA graph.
+
+        runner = StreamRunner(model, cache)
+        logits = runner.step(ids)     # ids [batch, q]; logits [batch, q, vocab]
+
+    A replayed step's logits tensor is overwritten by the next replay: consume it first.
+    `replays` counts the steps served by a replay."""
+
     def __init__(self, model, cache, use_graph: bool = True):
         self.model, self.cache = model, cache
-        self.v2 = isinstance(cache, SinkCacheV2)
-        self.use_graph = use_graph and isinstance(cache, (SinkCache, SinkCacheV2)) and torch.cuda.is_available()
-        self.graph = None
-        self.static_ids = self.static_logits = self.static_pos = None
-        self._key = None
+        self.use_graph = (bool(use_graph) and torch.cuda.is_available()
+                          and callable(getattr(cache, "graph_signature", None)))
         self.replays = 0
+        self._captured: _CapturedStep | None = None
         self._warmed = False
+
+    @property
+    def graph(self) -> torch.cuda.CUDAGraph | None:
+        """The graph of the current layout, if one has been captured."""
+        return None if self._captured is None else self._captured.graph
 
     @torch.no_grad()
     def step(self, ids: torch.Tensor) -> torch.Tensor:
-        """Feed ids [batch, q]; returns logits [batch, q, vocab].  One-token steps on a steady
-        cache are graph-replayed; anything else runs eagerly (and may reallocate the cache or
-        resize the region, which invalidates the graph: it is then recaptured).  When graphed,
-        the returned tensor is overwritten by the next step: consume it first."""
-        one = ids.shape[-1] == 1
-        if self.graph is not None and self._layout() != self._key:
-            self.graph = None
-        if self.graph is not None and one and self.cache.is_steady:
-            self.static_ids.copy_(ids)
-            if self.v2:
-                self.static_pos.fill_(self.cache.tokens_seen)
-            self.graph.replay()
-            self._advance()
-            self.replays += 1
-            return self.static_logits
-        if self.use_graph and one and self.cache.is_steady:
-            self._capture(ids)
-            self.graph.replay()  # capture records but does not execute: run this step now
-            return self.static_logits
-        return self.model(ids, past_key_values=self.cache, use_cache=True).logits
+        if not (self.use_graph and ids.shape[-1] == 1 and self.cache.is_steady):
+            return self.model(ids, past_key_values=self.cache, use_cache=True).logits
+        signature = self.cache.graph_signature()
+        captured = self._captured
+        if captured is None or captured.signature != signature:
+            self._captured = None  # free the old layout's graph before capturing the new one
+            return self._capture_and_run(ids, signature)
+        logits = captured.run(ids, self.cache.tokens_seen)
+        self.cache.note_replayed_step()
+        self.replays += 1
+        return logits
 
-    def _advance(self):
-        if self.v2:
-            self.cache.advance_after_replay()
-            return
-        for layer in self.cache.layers:
-            layer.tokens_seen += 1
-            layer.tokens_evicted += 1
-
-    def _layout(self):
-        ws = self.cache.workspace.buf
-        return ([(l._kbuf.data_ptr(), l._vbuf.data_ptr()) for l in self.cache.layers],
-                ws.data_ptr() if ws is not None else None,
-                self.cache.layout_key() if self.v2 else None)
-
-    def _capture(self, ids):
-        if not self._warmed:
-            # Libraries the model calls set themselves up on first use (cuBLAS handles,
-            # lazily loaded kernels), which cannot happen inside a capture.  A v2 cache is
-            # steady right after its fill, so the first step may be a capture: run one
-            # forward without the cache first (it leaves the cache untouched).
+    def _warm_up(self, ids: torch.Tensor) -> None:
+        """One forward without the cache on a side stream (the cache is left untouched)."""
+        side = torch.cuda.Stream(device=ids.device)
+        side.wait_stream(torch.cuda.current_stream(ids.device))
+        with torch.cuda.stream(side):
             self.model(ids, use_cache=False)
-            torch.cuda.synchronize()
-            self._warmed = True
-        self._key = self._layout()
-        self.static_ids = ids.clone()
+        torch.cuda.current_stream(ids.device).wait_stream(side)
+        torch.cuda.synchronize(ids.device)
+        self._warmed = True
+
+    def _capture_and_run(self, ids: torch.Tensor, signature) -> torch.Tensor:
+        """Capture this step and run it.  The capture executes the step's host code (the
+        cache's counters advance once, as in an eager step) but none of its kernels; the
+        replay that follows runs them."""
+        if not self._warmed:
+            self._warm_up(ids)
+        positions = None
         kwargs = {}
-        if self.v2:
-            self.static_pos = torch.full((ids.shape[0], 1), self.cache.tokens_seen, dtype=torch.long,
-                                         device=ids.device)
-            kwargs["position_ids"] = self.static_pos
-        self.graph = torch.cuda.CUDAGraph()
-        torch.cuda.synchronize()
-        with torch.cuda.graph(self.graph):
-            self.static_logits = self.model(self.static_ids, past_key_values=self.cache, use_cache=True,
-                                            **kwargs).logits
+        if getattr(self.cache, "absolute_positions", False):
+            positions = torch.full((ids.shape[0], 1), self.cache.tokens_seen, dtype=torch.long, device=ids.device)
+            kwargs["position_ids"] = positions
+        captured = _CapturedStep(signature, ids.clone(), positions)
+        torch.cuda.synchronize(ids.device)
+        with torch.cuda.graph(captured.graph):
+            captured.logits = self.model(captured.ids, past_key_values=self.cache, use_cache=True, **kwargs).logits
+        captured.graph.replay()
+        self._captured = captured
+        return captured.logits

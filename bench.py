@@ -17,6 +17,14 @@ with each step's q/k/v copied from pinned host memory and its output copied back
 Streams are independent: ranks split them with no collective on the hot path (weak
 scaling: 64 streams per GPU).  `--impl reference` times the reference's CPU path (the
 oracle port of it) on this host's cores instead.
+
+The line's `model` object carries the model-level half of the metric at the same world
+size (skip it with --no-model): a random-init Qwen3-0.6B with SinkCache(4, 1020) streamed
+token by token from position 0 through the CUDA-graph StreamRunner, one stream per GPU
+(tok/s, and the mean NLL against the reference's own CPU run of stream 0), and the same
+model with 32,768 slots and 32 streams split over the GPUs (strong scaling: tok/s and
+mean NLL of the same global streams at every world size).  Per-rank NLL sums and times
+are gathered with NCCL after the timed regions.
 """
 
 import argparse
@@ -568,10 +576,10 @@ def model_configs():
                      num_attention_heads=16, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
                      max_position_embeddings=40960, tie_word_embeddings=True, rms_norm_eps=1e-6)
     return {
-        # Qwen3-0.6B, sink 4 + window 1020, 1 stream
+        # Qwen3-0.6B, sink 4 + window 1020, one stream per GPU
         "qwen3-0.6b-1k": dict(cfg=lambda: Qwen3Config(**qwen3_06b), n_sink=4, window=1020, streams=1,
                               partition=False),
-        # config 3: Llama-3.2-1B (llama3 rope scaling), 1K slots, 8 streams
+        # Llama-3.2-1B (llama3 rope scaling), 1K slots, 8 streams per GPU
         "llama3.2-1b-1k": dict(cfg=lambda: LlamaConfig(
             vocab_size=128256, hidden_size=2048, intermediate_size=8192, num_hidden_layers=16,
             num_attention_heads=32, num_key_value_heads=8, head_dim=64, rope_theta=5e5,
@@ -579,10 +587,10 @@ def model_configs():
                           "high_freq_factor": 4.0, "original_max_position_embeddings": 8192},
             max_position_embeddings=131072, tie_word_embeddings=True, rms_norm_eps=1e-5),
             n_sink=4, window=1020, streams=8, partition=False),
-        # config 4: Qwen3-0.6B with 32,768 slots, 32 streams split over the GPUs (16 per wave)
+        # Qwen3-0.6B with 32,768 slots, 32 streams split over the GPUs (16 per wave)
         "qwen3-0.6b-32k": dict(cfg=lambda: Qwen3Config(**qwen3_06b), n_sink=4, window=32764, streams=32,
                                partition=True, wave=16),
-        # config 5: Qwen3-8B, 4,096 slots, 16 streams per GPU
+        # Qwen3-8B, 4,096 slots, 16 streams per GPU
         "qwen3-8b-4k": dict(cfg=lambda: Qwen3Config(
             vocab_size=151936, hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
             num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
@@ -591,43 +599,53 @@ def model_configs():
     }
 
 
+def build_model(spec: dict, device: torch.device, seed: int = 0):
+    """Random-init bf16 model on `device` with the registered sink attention backend; the
+    same seed gives the same weights on every rank."""
+    from transformers import AutoModelForCausalLM
+
+    from attention_sinks_b200 import register
+    torch.manual_seed(seed)
+    with torch.device(device):
+        return AutoModelForCausalLM.from_config(spec["cfg"](), attn_implementation=register(),
+                                                dtype=torch.bfloat16).eval()
+
+
 class ModelBench:
-    """One model replica and `streams` sink caches on one GPU, filled to the steady state
-    (v1: n_sink + window kept rows + one pending; v2: n_sink + window tokens seen) through
-    the layers' update with synthetic K/V, then streamed one token per step under the
-    CUDA-graph StreamRunner."""
+    """One model replica and a sink cache for the streams `ids` (global stream indices) on one
+    GPU, filled to the steady state (v1: n_sink + window kept rows + one pending; v2:
+    n_sink + window tokens seen) through the layers' update with synthetic K/V, then
+    streamed one token per step under the CUDA-graph StreamRunner.  Every stream's fill and
+    tokens come from generators seeded by its global index, so a stream's data does not
+    depend on how streams are split over GPUs or waves."""
 
-    def __init__(self, spec: dict, streams_: int, device: torch.device, seed: int, cache: str = "v1"):
-        from transformers import AutoModelForCausalLM
+    IDS = 64
 
-        from attention_sinks_b200 import SinkCache, SinkCacheV2, StreamRunner, register
-        name = register()
-        cfg = spec["cfg"]()
-        torch.manual_seed(seed)
-        with torch.device(device):
-            self.model = AutoModelForCausalLM.from_config(cfg, attn_implementation=name,
-                                                          dtype=torch.bfloat16).eval()
-        self.cfg, self.batch, self.device = cfg, streams_, device
+    def __init__(self, spec: dict, model, stream_ids: list[int], device: torch.device, cache: str = "v1"):
+        from attention_sinks_b200 import SinkCache, SinkCacheV2, StreamRunner
+        self.model, self.cfg, self.batch, self.device = model, model.config, len(stream_ids), device
         cls = SinkCacheV2 if cache == "v2" else SinkCache
         self.cache = cls.from_model(self.model, n_sink=spec["n_sink"], window=spec["window"])
-        hkv, d = cfg.num_key_value_heads, cfg.head_dim
+        hkv, d = self.cfg.num_key_value_heads, self.cfg.head_dim
         rows = spec["n_sink"] + spec["window"] + (0 if cache == "v2" else 1)
-        g = torch.Generator(device=device).manual_seed(seed)
+        gens = [torch.Generator(device=device).manual_seed(10_000 + s) for s in stream_ids]
         for layer in self.cache.layers:
             for r0 in range(0, rows, 4096):
                 n = min(4096, rows - r0)
-                k = torch.randn(streams_, hkv, n, d, device=device, generator=g).to(torch.bfloat16)
-                v = torch.randn(streams_, hkv, n, d, device=device, generator=g).to(torch.bfloat16)
+                k = torch.cat([torch.randn(1, hkv, n, d, device=device, generator=g) for g in gens]).bfloat16()
+                v = torch.cat([torch.randn(1, hkv, n, d, device=device, generator=g) for g in gens]).bfloat16()
                 layer.update(k, v)
         self.runner = StreamRunner(self.model, self.cache)
-        self.ids = torch.randint(0, cfg.vocab_size, (streams_, 64), device=device, generator=g)
-        self.nll = torch.zeros(streams_, device=device)
+        self.ids = torch.cat([torch.randint(0, self.cfg.vocab_size, (1, self.IDS), device=device,
+                                            generator=torch.Generator(device=device).manual_seed(20_000 + s))
+                              for s in stream_ids])
+        self.nll = torch.zeros(self.batch, device=device, dtype=torch.float64)
 
     def step(self, i: int) -> None:
         import torch.nn.functional as F
-        j = i % (self.ids.shape[1] - 1)
+        j = i % (self.IDS - 1)
         logits = self.runner.step(self.ids[:, j:j + 1])[:, -1]
-        self.nll += F.cross_entropy(logits.float(), self.ids[:, j + 1], reduction="none")
+        self.nll += F.cross_entropy(logits.float(), self.ids[:, j + 1], reduction="none").double()
 
     def cache_bytes(self) -> int:
         return sum(l._kbuf.numel() * l._kbuf.element_size() + l._vbuf.numel() * l._vbuf.element_size()
@@ -639,49 +657,152 @@ class ModelBench:
         return 3 * self.cfg.num_hidden_layers
 
 
-def run_model(args, workload: str) -> None:
+def stream_run(spec: dict, stream_ids: list[int], device: torch.device, steps: int, warmup: int,
+               cache: str = "v1", wave: int | None = None) -> dict:
+    """Steady-state streaming of this rank's streams in waves: per wave, `warmup` steps (the
+    first eviction, the graph capture, replays), then `steps` timed graph-replayed steps.
+    Returns this rank's seconds, tokens and NLL sum over the timed steps."""
     from attention_sinks_b200 import streams
-    spec = model_configs()[workload]
-    rank, world, local = streams.init_from_env("nccl")
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    total = spec["streams"] * (world if not spec["partition"] else 1)
-    mine = len(streams.shard(spec["streams"], rank, world)) if spec["partition"] else spec["streams"]
-    wave = spec.get("wave", mine)
-    waves = [min(wave, mine - w0) for w0 in range(0, mine, wave)]
-    elapsed, launches = 0.0, 0
-    for wi, nb in enumerate(waves):
-        bench = ModelBench(spec, nb, device, seed=1000 * rank + wi, cache=args.cache)
-        for i in range(args.warmup):  # eager steps (eviction starts), capture, replays
+    model = build_model(spec, device)
+    wave = wave or max(len(stream_ids), 1)
+    seconds, tokens, nll, launches, cache_gb = 0.0, 0, 0.0, 0, 0.0
+    for w0 in range(0, len(stream_ids), wave):
+        bench = ModelBench(spec, model, stream_ids[w0:w0 + wave], device, cache)
+        for i in range(warmup):
             bench.step(i)
         assert bench.cache.is_steady and bench.runner.graph is not None
+        bench.nll.zero_()
         torch.cuda.synchronize()
-        streams.barrier()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-        for i in range(args.steps):
-            bench.step(args.warmup + i)
+        for i in range(steps):
+            bench.step(warmup + i)
         end.record()
         end.synchronize()
-        elapsed += start.elapsed_time(end) / 1e3
-        launches += bench.step_kernels() * args.steps
+        bench.cache.check_status()
+        seconds += start.elapsed_time(end) / 1e3
+        tokens += bench.batch * steps
+        nll += float(bench.nll.sum())
+        launches += bench.step_kernels() * steps
         cache_gb = bench.cache_bytes() / 1e9
         del bench
         torch.cuda.empty_cache()
-    t_max = streams.reduce_max(elapsed)
-    tok = streams.reduce_sum([mine * args.steps])[0]
+    del model
+    torch.cuda.empty_cache()
+    streams.barrier()
+    return {"seconds": seconds, "tokens": tokens, "nll_sum": nll, "launches": launches, "cache_gb": cache_gb}
+
+
+def gather(local: dict) -> dict:
+    """Job totals over ranks (NCCL, off the hot path): max of the seconds, sums of the rest."""
+    from attention_sinks_b200 import streams
+    t = streams.reduce_max(local["seconds"])
+    tok, nll, launches = streams.reduce_sum([local["tokens"], local["nll_sum"], local["launches"]])
+    return {"seconds": t, "tokens": int(tok), "nll_sum": nll, "launches": int(launches)}
+
+
+def reference_stream_nll() -> dict:
+    """The reference's own CPU run of the streamed Qwen3-0.6B / SinkCache(4, 1020) workload
+    (committed fixture of tests/golden: mean NLL over 4,096 one-token steps)."""
+    with open(os.path.join(ROOT, "tests", "golden", "golden.json")) as f:
+        return json.load(f)["config1"]
+
+
+def stream_qwen3_1k(device: torch.device, rank: int, world: int, steps: int = 4096) -> dict:
+    """Qwen3-0.6B (random init, the weights of the reference fixture), SinkCache(4, 1020),
+    one stream per GPU streamed token by token from position 0 through StreamRunner, the NLL
+    of every next token buffered on the device (the shape of experiments/ppl.py:52-84).
+    Stream r is the uniform token sequence of seed 1 + r; stream 0 is the reference run's."""
+    import torch.nn.functional as F
+
+    from attention_sinks_b200 import SinkCache, StreamRunner, register, streams
+    from tests.golden import cases
+    model, _ = cases.qwen3_0_6b(0, attn=register())
+    model = model.to(device)
+    ids = torch.randint(0, 151936, (1, steps + 1), generator=torch.Generator().manual_seed(1 + rank)).to(device)
+    cache = SinkCache.from_model(model, n_sink=4, window=1020)
+    runner = StreamRunner(model, cache)
+    nll = torch.empty(steps, device=device)
+    steady_from = 1200  # steps before this one fill the cache, evict eagerly, capture
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    torch.cuda.synchronize()
+    streams.barrier()
+    ev[0].record()
+    with torch.inference_mode():
+        for t in range(steps):
+            if t == steady_from:
+                ev[1].record()
+            logits = runner.step(ids[:, t:t + 1])[0, -1]
+            nll[t] = F.cross_entropy(logits.float()[None], ids[0, t + 1:t + 2])
+    ev[2].record()
+    ev[2].synchronize()
+    cache.check_status()
+    whole, steady = ev[0].elapsed_time(ev[2]) / 1e3, ev[1].elapsed_time(ev[2]) / 1e3
+    own_mean = float(nll.double().mean())
+    t_whole, t_steady = streams.reduce_max(whole), streams.reduce_max(steady)
+    nll_sum = streams.reduce_sum([float(nll.double().sum())])[0]
+    ref = reference_stream_nll()
+    out = {"streams": world, "steps_per_stream": steps, "graph_replays_per_stream": runner.replays,
+           "tok_s_stream": round(world * steps / t_whole, 1),
+           "tok_s_steady": round(world * (steps - steady_from) / t_steady, 1),
+           "ms_per_token_steady": round(t_steady * 1e3 / (steps - steady_from), 3),
+           "mean_nll": round(nll_sum / (world * steps), 5)}
     if rank == 0:
-        line = {"metric": METRIC, "value": round(tok / t_max, 1), "unit": "tok/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_max * 1e3 / args.steps, 4),
+        out["stream0_mean_nll"] = round(own_mean, 5)
+        out["reference_stream0_mean_nll"] = round(ref["mean_nll"], 5)
+        out["stream0_rel_to_reference"] = float(f"{abs(own_mean - ref['mean_nll']) / ref['mean_nll']:.3e}")
+    del runner, cache, model
+    torch.cuda.empty_cache()
+    return out
+
+
+def model_leg(device: torch.device, rank: int, world: int, steps: int, warmup: int) -> dict:
+    """The model-level numbers of the metric at this world size: Qwen3-0.6B with 1,024 slots
+    streamed token by token from position 0 (tok/s, mean NLL against the reference's run),
+    and Qwen3-0.6B with 32,768 slots and 32 streams split over the ranks (strong scaling);
+    per-rank NLL sums and times gathered over NCCL."""
+    from attention_sinks_b200 import streams
+    out = {"qwen3-0.6b-1k": stream_qwen3_1k(device, rank, world)}
+    spec = model_configs()["qwen3-0.6b-32k"]
+    mine = list(streams.shard(spec["streams"], rank, world))
+    local = stream_run(spec, mine, device, steps, warmup, "v1", spec["wave"])
+    tot = gather(local)
+    out["qwen3-0.6b-32k"] = {
+        "streams_total": spec["streams"], "streams_per_gpu": len(mine),
+        "waves_per_gpu": -(-len(mine) // spec["wave"]), "steps_per_stream": steps,
+        "tok_s": round(tot["tokens"] / tot["seconds"], 1),
+        "ms_per_step": round(tot["seconds"] * 1e3 / (steps * -(-len(mine) // spec["wave"])), 3),
+        "mean_nll": round(tot["nll_sum"] / tot["tokens"], 6), "scaling": "strong",
+        "cache_gb_per_wave": round(local["cache_gb"], 2)}
+    return out
+
+
+def run_model(args, workload: str) -> None:
+    from attention_sinks_b200 import streams
+    spec = model_configs()[workload]
+    rank, world, local_rank = streams.init_from_env("nccl")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if spec["partition"]:
+        mine = list(streams.shard(spec["streams"], rank, world))
+    else:
+        mine = list(range(rank * spec["streams"], (rank + 1) * spec["streams"]))
+    local = stream_run(spec, mine, device, args.steps, args.warmup, args.cache, spec.get("wave"))
+    tot = gather(local)
+    if rank == 0:
+        total = spec["streams"] * (world if not spec["partition"] else 1)
+        line = {"metric": METRIC, "value": round(tot["tokens"] / tot["seconds"], 1), "unit": "tok/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(tot["seconds"] * 1e3 / args.steps, 4),
                 "higher_is_better": True, "scaling": "strong" if spec["partition"] else "weak",
                 "vs_baseline": None, "dtype": "bf16 model / fp32 K" if args.cache == "v1" else "bf16 model / bf16 K",
-                "data": "synthetic (random-init weights, "
-                "uniform tokens, cache filled to the steady state)",
-                "config": {"workload": workload, "cache": args.cache, "streams_total": total, "streams_per_gpu": mine,
-                           "waves_per_gpu": len(waves), "n_sink": spec["n_sink"], "window": spec["window"],
-                           "layers": model_configs()[workload]["cfg"]().num_hidden_layers,
-                           "cache_gb_per_wave": round(cache_gb, 2), "runner": "StreamRunner (CUDA graph)"},
-                "gpu_launches": launches}
+                "data": "synthetic (random-init weights, uniform tokens, cache filled to the steady state)",
+                "config": {"workload": workload, "cache": args.cache, "streams_total": total,
+                           "streams_per_gpu": len(mine), "waves_per_gpu": -(-len(mine) // (spec.get("wave") or len(mine))),
+                           "n_sink": spec["n_sink"], "window": spec["window"],
+                           "layers": spec["cfg"]().num_hidden_layers, "cache_gb_per_wave": round(local["cache_gb"], 2),
+                           "runner": "StreamRunner (CUDA graph)"},
+                "mean_nll": round(tot["nll_sum"] / tot["tokens"], 6), "gpu_launches": tot["launches"]}
         print(json.dumps(line), flush=True)
     streams.shutdown()
 
@@ -720,6 +841,10 @@ def main():
                     help="v1: SinkCache fused step (default); v2: SinkCacheV2 ring-buffer step")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the model-level leg (streamed tok/s and mean NLL of Qwen3-0.6B at 1K and 32K slots)")
+    ap.add_argument("--model-steps", type=int, default=32,
+                    help="timed steady steps per stream of the 32K-slot model leg")
     ap.add_argument("--workload", default="op", choices=["op", "chunk"] + sorted(model_configs()),
                     help="op: the layer-step (default); otherwise a model-level streamed run")
     args = ap.parse_args()
@@ -812,16 +937,19 @@ def main():
 
     launches = bench.launches_per_step() * args.steps
     plan = dict(bench.plan)
+    del bench
+    torch.cuda.empty_cache()
     extra = {}
     if world == 1 and rank == 0:
         if not args.no_sweep:
             flush = torch.empty(512 * 2 ** 20, dtype=torch.uint8, device=device)
-            del bench
-            torch.cuda.empty_cache()
             extra["sweep"] = sweep(device, flush, kind["cls"], alg)
             del flush
+            torch.cuda.empty_cache()
         if not args.no_cpu:
             extra["cpu_baseline"] = kind["cpu"](args.slots)
+    if not args.no_model:  # every rank: per-rank NLL sums and times are gathered over NCCL
+        extra["model"] = model_leg(device, rank, world, args.model_steps, args.warmup)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),

@@ -1,5 +1,5 @@
 """Streamed-NLL parity at model level against the reference's own CPU runs (fixtures):
-BASELINE config 1 (random-init Qwen3-0.6B, SinkCache(4, 1020), 4,096 one-token steps, so
+random-init Qwen3-0.6B with SinkCache(4, 1020) over 4,096 one-token steps (so
 eviction and re-rotation fire from step 1,025 on) and a Llama-3.2-shaped model (llama3
 rope scaling, head_dim 64, GQA 4, batch 2).  Both run the fused kernels under the
 CUDA-graph StreamRunner.  Target: mean NLL within 0.5 % of the reference's."""
@@ -17,7 +17,7 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-def test_config1_streamed_nll_matches_reference(golden, golden_arrays):
+def test_qwen3_streamed_nll_matches_reference(golden, golden_arrays):
     want_meta = golden["config1"]
     steps = want_meta["steps"]
     name = register()
@@ -33,7 +33,7 @@ def test_config1_streamed_nll_matches_reference(golden, golden_arrays):
     rel = abs(nll.mean().item() - want.mean().item()) / want.mean().item()
     rel_evicting = abs(nll[1024:].mean().item() - want[1024:].mean().item()) / want[1024:].mean().item()
     diff = (nll - want).abs()
-    print(f"config1: mean NLL {nll.mean():.5f} vs reference {want.mean():.5f} (rel {rel:.2e}; "
+    print(f"qwen3-0.6b 4+1020: mean NLL {nll.mean():.5f} vs reference {want.mean():.5f} (rel {rel:.2e}; "
           f"evicting steps rel {rel_evicting:.2e}); per-token |d| mean {diff.mean():.4f} max {diff.max():.4f}")
     assert rel < 5e-3 and rel_evicting < 5e-3
     assert cache.tokens_evicted == want_meta["tokens_evicted"]
