@@ -624,22 +624,46 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
     // them visible); each merges a slice of the pair's G * 128 outputs, as the combine
     // kernel would.  Partials are read through L2 (.cg).
     cluster_sync();
-    const int p = int(blockIdx.x) / A.ns, j = int(blockIdx.x) - p * A.ns;
+    const int ns = A.ns;
+    const int p = int(blockIdx.x) / ns, j = int(blockIdx.x) - p * ns;
     const int b = p / A.heads_kv, h = p - b * A.heads_kv;
-    const size_t base = size_t(p) * A.ns;
-    for (int idx = j * kTcThreads + tid; idx < G * kTcD; idx += A.ns * kTcThreads) {
-      const int g = idx / kTcD, d = idx - g * kTcD;
+    const size_t pb = size_t(p) * ns;
+    // The K ring is idle now: per group, the ns partials' maxima and sums (loaded in
+    // parallel, one per thread), turned into normalised weights by one thread per group.
+    float* wts = reinterpret_cast<float*>(gbase);  // [GMAX][kTcClusterMax]
+    float* mxs = wts + GMAX * kTcClusterMax;
+    for (int t = tid; t < G * ns; t += kTcThreads) {
+      const int g = t / ns, s = t - g * ns;
+      mxs[g * kTcClusterMax + s] = __ldcg(A.m_part + (pb + s) * G + g);
+      wts[g * kTcClusterMax + s] = __ldcg(A.l_part + (pb + s) * G + g);
+    }
+    __syncthreads();
+    if (tid < G) {
+      float* w = wts + tid * kTcClusterMax;
+      const float* m = mxs + tid * kTcClusterMax;
       float mx = kNegInf;
-      for (int s = 0; s < A.ns; ++s) mx = fmaxf(mx, __ldcg(A.m_part + (base + s) * G + g));
+      for (int s = 0; s < ns; ++s) mx = fmaxf(mx, m[s]);
       const float mref = mx == kNegInf ? 0.f : mx;
       float sum = 0.f;
-      for (int s = 0; s < A.ns; ++s)
-        sum = __fmaf_rn(exp2f(__ldcg(A.m_part + (base + s) * G + g) - mref), __ldcg(A.l_part + (base + s) * G + g), sum);
+      for (int s = 0; s < ns; ++s) sum = __fmaf_rn(exp2f(m[s] - mref), w[s], sum);
       const float inv = 1.f / sum;
+      for (int s = 0; s < ns; ++s) w[s] = exp2f(m[s] - mref) * inv;
+    }
+    __syncthreads();
+    // this CTA's equal slice of the pair's G * 128 outputs; an output's ns partials are
+    // all requested before any is used
+    const int per = (G * kTcD + ns - 1) / ns;
+    const int lo = j * per, hi = imin(lo + per, G * kTcD);
+    for (int idx = lo + tid; idx < hi; idx += kTcThreads) {
+      const int g = idx / kTcD, d = idx - g * kTcD;
+      float o_s[kTcClusterMax];
+#pragma unroll
+      for (int s = 0; s < kTcClusterMax; ++s)
+        o_s[s] = s < ns ? __ldcg(A.o_part + ((pb + s) * G + g) * kTcD + d) : 0.f;
       float o = 0.f;
-      for (int s = 0; s < A.ns; ++s)
-        o = __fmaf_rn(exp2f(__ldcg(A.m_part + (base + s) * G + g) - mref) * inv,
-                      __ldcg(A.o_part + ((base + s) * G + g) * kTcD + d), o);
+#pragma unroll
+      for (int s = 0; s < kTcClusterMax; ++s)
+        if (s < ns) o = __fmaf_rn(wts[g * kTcClusterMax + s], o_s[s], o);
       T* op = reinterpret_cast<T*>(A.out) + b * A.o_sb + (h * G + g) * A.o_sh;
       op[d] = Elem<T>::from_f(o);
     }

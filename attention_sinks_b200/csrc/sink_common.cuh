@@ -315,6 +315,13 @@ struct Elem<__half> {
   static __device__ __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
 };
 
+// Shared memory the stream kernel's end-of-split merge reuses from its stages: per-warp
+// partials (m, l, acc per group), then (clustered launches) the CTA's merged partial that
+// the other CTAs of its cluster read, and the cluster merge's weights and maxima.
+__host__ __device__ constexpr int merge_scratch_bytes(int warps, int groups, int D) {
+  return ((warps + 1) * groups * (D + 2) + 2 * groups * kClusterMax) * 4;
+}
+
 // Compile-time geometry of the stream kernel for one (K type, V type, head_dim).
 //   LPR lanes share one cache row: lane i of a row owns K dims [4i, 4i+4) and
 //   [D/2 + 4i, D/2 + 4i + 4) (the RoPE half-split partners) and V dims [8i, 8i + 8).
@@ -333,9 +340,8 @@ struct StreamGeom {
   static constexpr int S = S0 < 2 ? 2 : (S0 > 4 ? 4 : S0);
   static constexpr int HALO = kClusterHaloRows * (KROW + VROW);  // clustered launches' halo rows
   static constexpr int SMEM = kBarrierBytes + S * STAGE + HALO;
-  // the end-of-split merge reuses the stage memory: per-warp partials, then (clustered) the
-  // CTA's merged partial that the other CTAs of its cluster read
-  static_assert((kWarps + 1) * kMaxGroup * (D + 2) * 4 <= S * STAGE, "merge scratch");
+  // the end-of-split merge reuses the stage memory (merge_scratch_bytes)
+  static_assert(merge_scratch_bytes(kWarps, kMaxGroup, D) <= S * STAGE, "merge scratch");
   static_assert(kBarrierBytes >= 8 * (S + 1), "stage barriers and the halo barrier");
 };
 

@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
   constexpr int NT = 32 * NW;
   using Gm = StreamGeom<KT, VT, D>;
   using Lanes = StreamLanes<KT, VT, D, GMAX, ATTEND, NW>;
-  static_assert((NW + 1) * GMAX * (D + 2) * 4 <= Gm::S * Gm::STAGE, "merge scratch");
+  static_assert(merge_scratch_bytes(NW, GMAX, D) <= Gm::S * Gm::STAGE, "merge scratch");
   constexpr int T = Gm::T, S = Gm::S, KROW = Gm::KROW, STAGE = Gm::STAGE;
   constexpr int VROW = Gm::VROW;
 
@@ -180,6 +180,13 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
     for (int c = 0; c < pro; ++c) issue_chunk(c);
   }
 
+  // The rotation table and the group's queries (plain loads) are requested while the
+  // first chunks' copies are in flight, before any barrier.
+  Lanes L;
+  L.init(A);
+  L.begin_pair(A, b, h);
+  const uint8_t* mrow = A.mask != nullptr ? A.mask + b * A.mask_sb : nullptr;
+
   bool failed = false, halo_landed = !halo_issued;
   if (clustered) {
     // Every CTA of the cluster holds its halo rows before any CTA stores: a split reads the
@@ -191,11 +198,6 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
     }
     cluster_sync();
   }
-
-  Lanes L;
-  L.init(A);
-  L.begin_pair(A, b, h);
-  const uint8_t* mrow = A.mask != nullptr ? A.mask + b * A.mask_sb : nullptr;
 
 #pragma unroll 1
   for (int c = 0; c < nchunks; ++c) {
@@ -281,7 +283,8 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
       return;
     }
     // Clustered: this CTA's partial (O[g][d], then M[g], L[g]) stays in shared memory; after
-    // the barrier every CTA merges a slice of the pair's G * D outputs from all ns partials.
+    // the barrier every CTA merges an equal slice of the pair's G * D outputs from all ns
+    // partials, read through distributed shared memory.
     float* part = scratch + NW * GMAX * (D + 2);
     for (int idx = tid; idx < G * D; idx += NT) {
       const int g = idx / D, d = idx - g * D;
@@ -294,23 +297,48 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
       }
     }
     cluster_sync();
-    if (!failed) {
+    if (!failed) {  // CTA-uniform
+      const int ns = A.ns;
       const uint32_t part_addr = smem_addr(part);
-      for (int idx = j * NT + tid; idx < G * D; idx += A.ns * NT) {
-        const int g = idx / D, d = idx - g * D;
+      // Every partial's (M, L) per group, one remote load each, in parallel; then one thread
+      // per group turns them into normalised weights (the split combine's arithmetic).
+      float* wts = part + GMAX * (D + 2);   // [GMAX][kClusterMax]
+      float* mxs = wts + GMAX * kClusterMax;
+      for (int t = tid; t < G * ns; t += NT) {
+        const int g = t / ns, r = t - g * ns;
+        const uint32_t rb = cluster_map(part_addr, uint32_t(r));
+        mxs[g * kClusterMax + r] = ld_cluster_f32(rb + 4u * uint32_t(G * D + g));
+        wts[g * kClusterMax + r] = ld_cluster_f32(rb + 4u * uint32_t(G * D + G + g));
+      }
+      __syncthreads();
+      if (tid < G) {
+        float* w = wts + tid * kClusterMax;
+        const float* m = mxs + tid * kClusterMax;
         float mx = kNegInf;
-        for (int r = 0; r < A.ns; ++r)
-          mx = fmaxf(mx, ld_cluster_f32(cluster_map(part_addr + 4u * uint32_t(G * D + g), uint32_t(r))));
+        for (int r = 0; r < ns; ++r) mx = fmaxf(mx, m[r]);
         const float mref = mx == kNegInf ? 0.f : mx;
-        float sum = 0.f, o = 0.f;
-        for (int r = 0; r < A.ns; ++r) {
-          const uint32_t base = cluster_map(part_addr, uint32_t(r));
-          const float w = exp2f(ld_cluster_f32(base + 4u * uint32_t(G * D + g)) - mref);
-          sum = __fmaf_rn(w, ld_cluster_f32(base + 4u * uint32_t(G * D + G + g)), sum);
-          o = __fmaf_rn(w, ld_cluster_f32(base + 4u * uint32_t(idx)), o);
-        }
+        float sum = 0.f;
+        for (int r = 0; r < ns; ++r) sum = __fmaf_rn(exp2f(m[r] - mref), w[r], sum);
+        const float inv = 1.f / sum;
+        for (int r = 0; r < ns; ++r) w[r] = exp2f(m[r] - mref) * inv;
+      }
+      __syncthreads();
+      // This CTA's slice of the outputs: all ns remote partials of an output are requested
+      // before any is used, so the slice costs about one round trip.
+      const int per = (G * D + ns - 1) / ns;
+      const int lo = j * per, hi = imin(lo + per, G * D);
+      for (int idx = lo + tid; idx < hi; idx += NT) {
+        const int g = idx / D, d = idx - g * D;
+        float o_r[kClusterMax];
+#pragma unroll
+        for (int r = 0; r < kClusterMax; ++r)
+          o_r[r] = r < ns ? ld_cluster_f32(cluster_map(part_addr, uint32_t(r)) + 4u * uint32_t(idx)) : 0.f;
+        float o = 0.f;
+#pragma unroll
+        for (int r = 0; r < kClusterMax; ++r)
+          if (r < ns) o = __fmaf_rn(wts[g * kClusterMax + r], o_r[r], o);
         VT* op = reinterpret_cast<VT*>(A.out) + b * A.o_sb + (h * G + g) * A.o_sh;
-        op[d] = Elem<VT>::from_f(o / sum);
+        op[d] = Elem<VT>::from_f(o);
       }
     }
     cluster_sync();  // no CTA leaves while another still reads its partial

@@ -318,7 +318,7 @@ int32_t launch_dependent(void (*kern)(Params...), dim3 grid, int smem, cudaStrea
 template <typename KT, typename VT, int D, int GMAX>
 constexpr int cluster_warps() {
   using Gm = StreamGeom<KT, VT, D>;
-  return 9 * GMAX * (D + 2) * 4 <= Gm::S * Gm::STAGE ? 8 : 4;
+  return merge_scratch_bytes(8, GMAX, D) <= Gm::S * Gm::STAGE ? 8 : 4;
 }
 
 // Failure-detection test hook (sink_debug_fail_next_wait): armed as (chunk << 32) | polls,
