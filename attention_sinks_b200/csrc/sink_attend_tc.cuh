@@ -248,9 +248,6 @@ __device__ __forceinline__ bool tc_softmax_or(bool pred) {  // OR over the 128 s
   return r != 0;
 }
 __device__ __forceinline__ void tc_softmax_sync() { asm volatile("barrier.cta.sync 1, 128;" ::: "memory"); }
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
 
 template <typename T, int GMAX>
 __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __grid_constant__ TcArgs A) {
@@ -629,7 +626,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
     const int b = p / A.heads_kv, h = p - b * A.heads_kv;
     const size_t pb = size_t(p) * ns;
     // The K ring is idle now: per group, the ns partials' maxima and sums (loaded in
-    // parallel, one per thread), turned into normalised weights by one thread per group.
+    // parallel, one per thread), turned into normalised weights by one warp per group.
     float* wts = reinterpret_cast<float*>(gbase);  // [GMAX][kTcClusterMax]
     float* mxs = wts + GMAX * kTcClusterMax;
     for (int t = tid; t < G * ns; t += kTcThreads) {
@@ -638,16 +635,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
       wts[g * kTcClusterMax + s] = __ldcg(A.l_part + (pb + s) * G + g);
     }
     __syncthreads();
-    if (tid < G) {
-      float* w = wts + tid * kTcClusterMax;
-      const float* m = mxs + tid * kTcClusterMax;
-      float mx = kNegInf;
-      for (int s = 0; s < ns; ++s) mx = fmaxf(mx, m[s]);
-      const float mref = mx == kNegInf ? 0.f : mx;
-      float sum = 0.f;
-      for (int s = 0; s < ns; ++s) sum = __fmaf_rn(exp2f(m[s] - mref), w[s], sum);
-      const float inv = 1.f / sum;
-      for (int s = 0; s < ns; ++s) w[s] = exp2f(m[s] - mref) * inv;
+    for (int g = warp; g < G; g += kTcThreads / 32) {  // one warp per group, one split per lane
+      const bool live = lane < ns;
+      const float w = split_weight(live ? mxs[g * kTcClusterMax + lane] : kNegInf,
+                                   live ? wts[g * kTcClusterMax + lane] : 0.f);
+      __syncwarp();
+      if (live) wts[g * kTcClusterMax + lane] = w;
     }
     __syncthreads();
     // this CTA's equal slice of the pair's G * 128 outputs; an output's ns partials are

@@ -14,6 +14,23 @@ namespace sinkb200 {
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr float kNegInf = -__builtin_inff();
 
+// Normalised softmax weight of split `lane` of one query row in a merge of ns <= 32 split
+// partials, one split per lane (lanes >= ns pass m = -inf, l = 0): exp2(m - max) divided by
+// sum over splits of exp2(m_s - max) * l_s.  The maximum and the sum are reduced over the
+// whole warp in the same butterfly order as sink_combine_kernel, so an in-cluster merge gets
+// the same weights as the combine launch.
+__device__ __forceinline__ float split_weight(float m, float l) {
+  float mx = m;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
+  const float mref = mx == kNegInf ? 0.f : mx;
+  const float e = exp2f(m - mref);
+  float sum = __fmaf_rn(e, l, 0.f);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(kFull, sum, off);
+  return e * (1.f / sum);
+}
+
 // NW warps per CTA share each chunk: warp w takes row groups w, w + NW, ... (T / (NW * RPW)
 // steps of RPW rows).  The chunk geometry (T rows) does not depend on NW.
 template <typename KT, typename VT, int D, int GMAX, bool ATTEND, int NW = kWarps>

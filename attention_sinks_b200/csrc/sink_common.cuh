@@ -119,6 +119,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
+// Adds `bytes` to the transaction count the current phase waits for (no arrival).
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -201,6 +211,17 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
+}
+// Split cluster barrier: arrive (release) and wait (acquire) as two steps, so a CTA can keep
+// working between its arrival and the point where it needs the other CTAs' arrivals.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
   float v;
@@ -315,11 +336,17 @@ struct Elem<__half> {
   static __device__ __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
 };
 
-// Shared memory the stream kernel's end-of-split merge reuses from its stages: per-warp
-// partials (m, l, acc per group), then (clustered launches) the CTA's merged partial that
-// the other CTAs of its cluster read, and the cluster merge's weights and maxima.
+// Shared memory the stream kernel's end-of-split merge reuses from its stages: the per-warp
+// partials (m, l, acc per group).
 __host__ __device__ constexpr int merge_scratch_bytes(int warps, int groups, int D) {
-  return ((warps + 1) * groups * (D + 2) + 2 * groups * kClusterMax) * 4;
+  return warps * groups * (D + 2) * 4;
+}
+
+// Floats of a clustered launch's merge area: the pair's G * D outputs split into ns equal
+// slices, one slice per CTA, each received from every CTA (ns * ceil(G * D / ns) <=
+// G * D + ns - 1 floats), then every CTA's (M, L) per group, and the merge weights.
+__host__ __device__ constexpr int cluster_merge_floats(int groups, int D) {
+  return groups * D + kClusterMax + 3 * groups * kClusterMax;
 }
 
 // Compile-time geometry of the stream kernel for one (K type, V type, head_dim).
@@ -339,7 +366,11 @@ struct StreamGeom {
   static constexpr int S0 = kPipeBytes / STAGE;
   static constexpr int S = S0 < 2 ? 2 : (S0 > 4 ? 4 : S0);
   static constexpr int HALO = kClusterHaloRows * (KROW + VROW);  // clustered launches' halo rows
-  static constexpr int SMEM = kBarrierBytes + S * STAGE + HALO;
+  // clustered launches' merge area: the split partials other CTAs of the cluster push here
+  static constexpr int MERGE = cluster_merge_floats(kMaxGroup, D) * 4;
+  // what the split planner counts per CTA (CTAs per SM), and what a launch opts into
+  static constexpr int PLAN_SMEM = kBarrierBytes + S * STAGE + HALO;
+  static constexpr int SMEM = PLAN_SMEM + MERGE;
   // the end-of-split merge reuses the stage memory (merge_scratch_bytes)
   static_assert(merge_scratch_bytes(kWarps, kMaxGroup, D) <= S * STAGE, "merge scratch");
   static_assert(kBarrierBytes >= 8 * (S + 1), "stage barriers and the halo barrier");

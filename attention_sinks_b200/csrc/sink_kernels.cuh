@@ -23,51 +23,40 @@ namespace sinkb200 {
 // four contiguous segments (unshifted rows below the window; window rows shifted by drop,
 // read directly below the halo range, from the halo copy `hk`/`hv` (row hlo first), and
 // directly above it).  With no halo copy given, rows whose source lies in [hlo, hhi) are
-// left for the caller to fill.  The append row is filled by threads.  One arrival with the
-// chunk's byte count completes the stage barrier's phase.
+// left for the caller to fill.  The append row is filled by threads.  Each segment adds its
+// bytes to the stage barrier's expected count before its copies are issued, and one
+// arrival at the end lets the phase complete once every byte has landed.
 template <typename KT, typename VT, int D>
 __device__ __forceinline__ void issue_rows(const StreamArgs& A, const KT* kb, const VT* vb, int x,
                                            int xe, int hlo, int hhi, const unsigned char* hk,
                                            const unsigned char* hv, uint32_t sk, uint32_t sv,
                                            uint32_t bar) {
   constexpr int KROW = D * (int)sizeof(KT), VROW = D * (int)sizeof(VT);
-  int seg_t[4], seg_n[4];
-  const void* seg_k[4];
-  const void* seg_v[4];
-  int nseg = 0;
-  auto add = [&](int t, int n, const void* k, const void* v) {
-    seg_t[nseg] = t;
-    seg_n[nseg] = n;
-    seg_k[nseg] = k;
-    seg_v[nseg] = v;
-    ++nseg;
+  auto segment = [&](int t, int n, const void* k, const void* v) {
+    mbar_expect_tx(bar, uint32_t(n) * (KROW + VROW));
+    bulk_g2s(sk + t * KROW, k, uint32_t(n) * KROW, bar);
+    bulk_g2s(sv + t * VROW, v, uint32_t(n) * VROW, bar);
   };
   const int lowlim = A.drop > 0 ? A.n_sink : (A.append_row >= 0 ? A.append_row : A.row_end);
   const int p1 = imin(xe, lowlim);
-  if (x < p1) add(0, p1 - x, kb + size_t(x) * D, vb + size_t(x) * D);
+  if (x < p1) segment(0, p1 - x, kb + size_t(x) * D, vb + size_t(x) * D);
   if (A.drop > 0) {
     const int w0 = imax(x, A.n_sink), w1 = imin(xe, A.n_sink + A.window);
     if (w0 < w1) {
       const int s0 = w0 + A.drop, s1 = w1 + A.drop;
       const bool halo = hlo < hhi;
       const int d1 = halo ? imin(s1, hlo) : s1;
-      if (s0 < d1) add(s0 - A.drop - x, d1 - s0, kb + size_t(s0) * D, vb + size_t(s0) * D);
+      if (s0 < d1) segment(s0 - A.drop - x, d1 - s0, kb + size_t(s0) * D, vb + size_t(s0) * D);
       if (halo) {
         const int h0 = imax(s0, hlo), h1 = imin(s1, hhi);
         if (hk != nullptr && h0 < h1)
-          add(h0 - A.drop - x, h1 - h0, hk + size_t(h0 - hlo) * KROW, hv + size_t(h0 - hlo) * VROW);
+          segment(h0 - A.drop - x, h1 - h0, hk + size_t(h0 - hlo) * KROW, hv + size_t(h0 - hlo) * VROW);
         const int u0 = imax(s0, hhi);
-        if (u0 < s1) add(u0 - A.drop - x, s1 - u0, kb + size_t(u0) * D, vb + size_t(u0) * D);
+        if (u0 < s1) segment(u0 - A.drop - x, s1 - u0, kb + size_t(u0) * D, vb + size_t(u0) * D);
       }
     }
   }
-  uint32_t bytes = 0;
-  for (int i = 0; i < nseg; ++i) bytes += uint32_t(seg_n[i]) * (KROW + VROW);
-  mbar_arrive_expect_tx(bar, bytes);
-  for (int i = 0; i < nseg; ++i) {
-    bulk_g2s(sk + seg_t[i] * KROW, seg_k[i], uint32_t(seg_n[i]) * KROW, bar);
-    bulk_g2s(sv + seg_t[i] * VROW, seg_v[i], uint32_t(seg_n[i]) * VROW, bar);
-  }
+  mbar_arrive(bar);
 }
 
 // Rows of [x, xe) this step writes back: window rows (drop > 0) and the append row.
@@ -190,13 +179,14 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
   bool failed = false, halo_landed = !halo_issued;
   if (clustered) {
     // Every CTA of the cluster holds its halo rows before any CTA stores: a split reads the
-    // first rows of the next split before that split overwrites them.  Only loads precede
-    // this barrier.
+    // first rows of the next split before that split overwrites them.  A CTA arrives once
+    // its halo rows have landed and waits for the others' arrivals only before its first
+    // store (after the first chunk's work), so the barrier's latency overlaps that work.
     if (halo_issued) {
       halo_landed = mbar_wait_bounded(halo_bar, 0, polls);
       if (!halo_landed) failed = true;
     }
-    cluster_sync();
+    cluster_arrive();
   }
 
 #pragma unroll 1
@@ -230,6 +220,7 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
     store_range(A, x, xe, st_lo, st_hi);
     fence_proxy_async_smem();
     failed = __syncthreads_or(failed);
+    if (clustered && c == 0) cluster_wait();  // every halo of the cluster has landed
     if (tid == 0) {
       if (!failed && st_lo < st_hi) {
         bulk_s2g(kb + size_t(st_lo) * D, smem_addr(sk) + (st_lo - x) * KROW, uint32_t(st_hi - st_lo) * KROW);
@@ -243,7 +234,8 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
       }
     }
   }
-  if (tid == 0) bulk_wait<0>();
+  // The stores have read their shared memory (their global writes complete with the grid).
+  if (tid == 0) bulk_wait_read<0>();
   failed = __syncthreads_or(failed);
   allow_dependents();
   if (failed && tid == 0) {
@@ -282,66 +274,50 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
       }
       return;
     }
-    // Clustered: this CTA's partial (O[g][d], then M[g], L[g]) stays in shared memory; after
-    // the barrier every CTA merges an equal slice of the pair's G * D outputs from all ns
-    // partials, read through distributed shared memory.
-    float* part = scratch + NW * GMAX * (D + 2);
+    // Clustered: the pair's G * D outputs are cut into ns equal slices, slice r merged by
+    // the CTA of rank r.  Every CTA pushes each output of its partial into the owning CTA's
+    // merge area (remote stores, no round trip) and its (M, L) per group into every CTA's;
+    // after one cluster barrier each CTA merges its slice from its own shared memory.
+    const int ns = A.ns;
+    const int per = (G * D + ns - 1) / ns;
+    float* recv_o = reinterpret_cast<float*>(halo_sv + kClusterHaloRows * VROW);  // [ns][per]
+    float* recv_m = recv_o + GMAX * D + kClusterMax;                            // [GMAX][kClusterMax]
+    float* recv_l = recv_m + GMAX * kClusterMax;
+    float* wts = recv_l + GMAX * kClusterMax;
+    const uint32_t o_addr = smem_addr(recv_o), m_addr = smem_addr(recv_m), l_addr = smem_addr(recv_l);
     for (int idx = tid; idx < G * D; idx += NT) {
       const int g = idx / D, d = idx - g * D;
       float M, Ls, O;
       Lanes::from_scratch(scratch, g, d, M, Ls, O);
-      part[idx] = O;
+      const int owner = idx / per;
+      st_cluster_f32(cluster_map(o_addr + 4u * uint32_t(j * per + idx - owner * per), uint32_t(owner)), O);
       if (d == 0) {
-        part[G * D + g] = M;
-        part[G * D + G + g] = Ls;
+        for (int r = 0; r < ns; ++r) {
+          st_cluster_f32(cluster_map(m_addr + 4u * uint32_t(g * kClusterMax + j), uint32_t(r)), M);
+          st_cluster_f32(cluster_map(l_addr + 4u * uint32_t(g * kClusterMax + j), uint32_t(r)), Ls);
+        }
       }
     }
-    cluster_sync();
-    if (!failed) {  // CTA-uniform
-      const int ns = A.ns;
-      const uint32_t part_addr = smem_addr(part);
-      // Every partial's (M, L) per group, one remote load each, in parallel; then one thread
-      // per group turns them into normalised weights (the split combine's arithmetic).
-      float* wts = part + GMAX * (D + 2);   // [GMAX][kClusterMax]
-      float* mxs = wts + GMAX * kClusterMax;
-      for (int t = tid; t < G * ns; t += NT) {
-        const int g = t / ns, r = t - g * ns;
-        const uint32_t rb = cluster_map(part_addr, uint32_t(r));
-        mxs[g * kClusterMax + r] = ld_cluster_f32(rb + 4u * uint32_t(G * D + g));
-        wts[g * kClusterMax + r] = ld_cluster_f32(rb + 4u * uint32_t(G * D + G + g));
+    cluster_sync();  // every push has landed; after this no CTA touches another's memory
+    if (!failed) {   // CTA-uniform
+      // normalised weights: one warp per group, one split per lane
+      const int lane = tid & 31;
+      for (int g = tid >> 5; g < G; g += NW) {
+        const bool live = lane < ns;
+        const float w = split_weight(live ? recv_m[g * kClusterMax + lane] : kNegInf,
+                                     live ? recv_l[g * kClusterMax + lane] : 0.f);
+        if (live) wts[g * kClusterMax + lane] = w;
       }
       __syncthreads();
-      if (tid < G) {
-        float* w = wts + tid * kClusterMax;
-        const float* m = mxs + tid * kClusterMax;
-        float mx = kNegInf;
-        for (int r = 0; r < ns; ++r) mx = fmaxf(mx, m[r]);
-        const float mref = mx == kNegInf ? 0.f : mx;
-        float sum = 0.f;
-        for (int r = 0; r < ns; ++r) sum = __fmaf_rn(exp2f(m[r] - mref), w[r], sum);
-        const float inv = 1.f / sum;
-        for (int r = 0; r < ns; ++r) w[r] = exp2f(m[r] - mref) * inv;
-      }
-      __syncthreads();
-      // This CTA's slice of the outputs: all ns remote partials of an output are requested
-      // before any is used, so the slice costs about one round trip.
-      const int per = (G * D + ns - 1) / ns;
       const int lo = j * per, hi = imin(lo + per, G * D);
       for (int idx = lo + tid; idx < hi; idx += NT) {
-        const int g = idx / D, d = idx - g * D;
-        float o_r[kClusterMax];
-#pragma unroll
-        for (int r = 0; r < kClusterMax; ++r)
-          o_r[r] = r < ns ? ld_cluster_f32(cluster_map(part_addr, uint32_t(r)) + 4u * uint32_t(idx)) : 0.f;
+        const int g = idx / D, d = idx - g * D, i = idx - lo;
         float o = 0.f;
-#pragma unroll
-        for (int r = 0; r < kClusterMax; ++r)
-          if (r < ns) o = __fmaf_rn(wts[g * kClusterMax + r], o_r[r], o);
+        for (int r = 0; r < ns; ++r) o = __fmaf_rn(wts[g * kClusterMax + r], recv_o[r * per + i], o);
         VT* op = reinterpret_cast<VT*>(A.out) + b * A.o_sb + (h * G + g) * A.o_sh;
         op[d] = Elem<VT>::from_f(o);
       }
     }
-    cluster_sync();  // no CTA leaves while another still reads its partial
   }
 }
 

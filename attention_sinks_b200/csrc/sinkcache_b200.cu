@@ -334,7 +334,7 @@ int32_t launch_stream(const StreamArgs& A0, const Plan& pl, int pairs, cudaStrea
     A.wait_polls = int(inject & 0x7fffffff);
   }
   using Gm = StreamGeom<KT, VT, D>;
-  if (Gm::SMEM != pl.smem || Gm::T != pl.T) return SINK_EINVAL;  // host/device geometry drift
+  if (Gm::PLAN_SMEM != pl.smem || Gm::T != pl.T) return SINK_EINVAL;  // host/device geometry drift
   // clustered launches (one CTA per SM in the latency regime) run 8 warps per CTA where the
   // merge scratch of 8 warps fits the stage memory
   constexpr int NWC = cluster_warps<KT, VT, D, GMAX>();
@@ -343,8 +343,8 @@ int32_t launch_stream(const StreamArgs& A0, const Plan& pl, int pairs, cudaStrea
   const int32_t rc = prepare_device(dev);
   if (rc) return rc;
   if (pl.cluster && (pl.ns > kClusterMax || A.cluster != 1)) return SINK_EINVAL;
-  // only clustered launches stage halo rows in shared memory
-  const int smem = pl.cluster ? Gm::SMEM : Gm::SMEM - Gm::HALO;
+  // only clustered launches stage halo rows and receive the cluster's partials in shared memory
+  const int smem = pl.cluster ? Gm::SMEM : Gm::SMEM - Gm::HALO - Gm::MERGE;
   return launch_dependent_c(kern, dim3(pl.ns, pairs), threads, smem, pl.cluster ? pl.ns : 1, st, A);
 }
 
