@@ -24,8 +24,9 @@ EXPORTED_SYMBOLS = (
     "sink_abi_version", "sink_strerror", "sink_workspace_bytes", "sink_plan", "sink_append",
     "sink_evict_rerotate", "sink_decode_attention", "sink_fused_decode_step", "sink_read_status",
     "sink_decode_attention_noalloc", "sink_v2_place", "sink_v2_decode_step", "sink_prepare_device",
-    "sink_debug_fail_next_wait",
+    "sink_debug_fail_next_wait", "sink_plan_launch",
 )
+LAUNCH_SPLIT, LAUNCH_CLUSTER, LAUNCH_TENSOR = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 16 << 20
 # argument errors (negative return codes of the C ABI)
 EINVAL, EDTYPE, EHEADDIM, EGROUP, ELAYOUT, EWORKSPACE, EDEVICE, ESCRATCH = -1, -2, -3, -4, -5, -6, -7, -8
@@ -65,6 +66,7 @@ def _declare(lib):
         "sink_strerror": (ctypes.c_char_p, [i32]),
         "sink_workspace_bytes": (sz, [i32] * 12),
         "sink_plan": (i32, [i32] * 12 + [pi32] * 6),
+        "sink_plan_launch": (i32, [i32] * 12 + [pi32] * 2),
         "sink_append": (i32, [pkv, prows, prows, i32, vp]),
         "sink_evict_rerotate": (i32, [pkv, i32, i32, i32, fp, fp, i32, vp, sz, vp]),
         "sink_decode_attention": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
@@ -199,7 +201,13 @@ def plan(op: int, batch: int, heads_kv: int, heads_q: int, head_dim: int, k_dtyp
                          rows, n_sink, window, drop, num_sms, *[ctypes.byref(o) for o in out])
     _check(rc, "sink_plan")
     keys = ("splits", "rows_per_split", "chunk_rows", "stages", "smem_bytes", "cluster_ctas")
-    return {k: o.value for k, o in zip(keys, out)}
+    res = {k: o.value for k, o in zip(keys, out)}
+    mode, ctas = ctypes.c_int32(), ctypes.c_int32()
+    rc = lib().sink_plan_launch(op, batch, heads_kv, heads_q, head_dim, dtype_code(k_dtype), dtype_code(v_dtype),
+                                rows, n_sink, window, drop, num_sms, ctypes.byref(mode), ctypes.byref(ctas))
+    _check(rc, "sink_plan_launch")
+    res["launch"], res["ctas"] = mode.value, ctas.value
+    return res
 
 
 class Workspace:

@@ -65,6 +65,12 @@ struct StreamLanes {
   // Start a new (batch, kv-head) pair: zero the softmax state, load the group's queries
   // pre-scaled by scale * log2(e).
   __device__ __forceinline__ void begin_pair(const StreamArgs& A, int b, int h) {
+    reset_softmax();
+    load_queries(A, b, h);
+  }
+
+  // Zero the online-softmax state (a new item of the same pair).
+  __device__ __forceinline__ void reset_softmax() {
     if constexpr (ATTEND) {
 #pragma unroll
       for (int g = 0; g < GMAX; ++g) {
@@ -72,6 +78,14 @@ struct StreamLanes {
         l[g] = 0.f;
 #pragma unroll
         for (int k = 0; k < 8; ++k) acc[g][k] = 0.f;
+      }
+    }
+  }
+
+  __device__ __forceinline__ void load_queries(const StreamArgs& A, int b, int h) {
+    if constexpr (ATTEND) {
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g) {
         if (g < A.group) {
           const VT* qp = reinterpret_cast<const VT*>(A.q) + b * A.q_sb + (h * A.group + g) * A.q_sh;
           float t4[4];

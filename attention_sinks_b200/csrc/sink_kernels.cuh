@@ -365,7 +365,12 @@ __global__ void __launch_bounds__(kThreads) sink_halo_kernel(const __grid_consta
   }
 }
 
-// Log-sum-exp merge of the ns split partials of every (batch, kv-head) pair.
+// Log-sum-exp merge of the ns split partials of every (batch, kv-head) pair.  Grid
+// (pairs, G * D / 32): a CTA merges 32 consecutive outputs of one query row g (D is a
+// multiple of 32).  Warp 0 turns the ns (max, sum) pairs of row g into normalised weights;
+// then, with more than 32 splits, the 4 warps each sum every 4th split's partial (lane =
+// output, coalesced) and the 4 sums are added in warp order; with at most 32 splits warp 0
+// sums them all in split order.  Either way the result does not depend on scheduling.
 template <typename VT, int D>
 __global__ void __launch_bounds__(kThreads) sink_combine_kernel(const float* __restrict__ o_part,
                                                                 const float* __restrict__ m_part,
@@ -373,13 +378,16 @@ __global__ void __launch_bounds__(kThreads) sink_combine_kernel(const float* __r
                                                                 char* out, int64_t o_sb,
                                                                 int64_t o_sh, int heads_kv, int G,
                                                                 int ns) {
-  __shared__ float wts[kMaxSplits * kMaxGroup];
+  __shared__ float wts[kMaxSplits];
+  __shared__ float sums[kWarps][32];
   grid_dependency_wait();  // the partials of the stream kernel are complete
   const int p = blockIdx.x;
   const int b = p / heads_kv, h = p - b * heads_kv;
+  const int first = blockIdx.y * 32;  // first output (g * D + d) of this CTA
+  const int g = first / D;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t base = size_t(p) * ns;
-  for (int g = warp; g < G; g += kWarps) {
+  if (warp == 0) {
     float mx = kNegInf;
     for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, m_part[(base + s) * G + g]);
 #pragma unroll
@@ -391,14 +399,20 @@ __global__ void __launch_bounds__(kThreads) sink_combine_kernel(const float* __r
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(kFull, sum, off);
     const float inv = 1.f / sum;
-    for (int s = lane; s < ns; s += 32)
-      wts[s * G + g] = exp2f(m_part[(base + s) * G + g] - mref) * inv;
+    for (int s = lane; s < ns; s += 32) wts[s] = exp2f(m_part[(base + s) * G + g] - mref) * inv;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
-    const int g = idx / D, d = idx - g * D;
+  const int d = first - g * D + lane;
+  const int nsub = ns > 32 ? kWarps : 1;
+  if (warp < nsub) {
     float o = 0.f;
-    for (int s = 0; s < ns; ++s) o = __fmaf_rn(wts[s * G + g], o_part[((base + s) * G + g) * D + d], o);
+    for (int s = warp; s < ns; s += nsub) o = __fmaf_rn(wts[s], o_part[((base + s) * G + g) * D + d], o);
+    sums[warp][lane] = o;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float o = sums[0][lane];
+    for (int w = 1; w < nsub; ++w) o += sums[w][lane];
     VT* op = reinterpret_cast<VT*>(out) + b * o_sb + (h * G + g) * o_sh;
     op[d] = Elem<VT>::from_f(o);
   }

@@ -390,15 +390,15 @@ template <typename VT>
 int32_t launch_combine_t(int D, const StreamArgs& A, int pairs, cudaStream_t st) {
   switch (D) {
     case 64:
-      return launch_dependent(sink_combine_kernel<VT, 64>, dim3(pairs), 0, st, (const float*)A.o_part,
+      return launch_dependent(sink_combine_kernel<VT, 64>, dim3(pairs, A.group * 64 / 32), 0, st, (const float*)A.o_part,
                               (const float*)A.m_part, (const float*)A.l_part, A.out, A.o_sb, A.o_sh,
                               A.heads_kv, A.group, A.ns);
     case 128:
-      return launch_dependent(sink_combine_kernel<VT, 128>, dim3(pairs), 0, st, (const float*)A.o_part,
+      return launch_dependent(sink_combine_kernel<VT, 128>, dim3(pairs, A.group * 128 / 32), 0, st, (const float*)A.o_part,
                               (const float*)A.m_part, (const float*)A.l_part, A.out, A.o_sb, A.o_sh,
                               A.heads_kv, A.group, A.ns);
     case 256:
-      return launch_dependent(sink_combine_kernel<VT, 256>, dim3(pairs), 0, st, (const float*)A.o_part,
+      return launch_dependent(sink_combine_kernel<VT, 256>, dim3(pairs, A.group * 256 / 32), 0, st, (const float*)A.o_part,
                               (const float*)A.m_part, (const float*)A.l_part, A.out, A.o_sb, A.o_sh,
                               A.heads_kv, A.group, A.ns);
     default: return SINK_EHEADDIM;
@@ -817,8 +817,7 @@ cudaError_t allow_smem_d() {
     if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 1, false, cluster_warps<KT, VT, D, 1>()>, bytes);
     return e;
   } else {
-    cudaError_t e = cudaSuccess;
-    if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 1, true, 4>, bytes);
+    cudaError_t e = stream_attrs(sink_stream_kernel<KT, VT, D, 1, true, 4>, bytes);
     if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 2, true, 4>, bytes);
     if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 4, true, 4>, bytes);
     if (e == cudaSuccess) e = stream_attrs(sink_stream_kernel<KT, VT, D, 8, true, 4>, bytes);
@@ -950,6 +949,29 @@ int32_t sink_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
   if (stages) *stages = pl.S;
   if (smem_bytes) *smem_bytes = pl.smem;
   if (cluster_ctas) *cluster_ctas = pl.cluster ? pl.ns : 1;
+  return SINK_OK;
+}
+
+int32_t sink_plan_launch(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q,
+                         int32_t head_dim, int32_t k_dtype, int32_t v_dtype, int32_t rows,
+                         int32_t n_sink, int32_t window, int32_t drop, int32_t num_sms,
+                         int32_t* mode, int32_t* ctas) {
+  Plan pl;
+  const int32_t rc = make_plan(op, batch, heads_kv, heads_q, head_dim, k_dtype, v_dtype, rows,
+                               n_sink, window, drop, num_sms, pl);
+  if (rc != SINK_OK) return rc;
+  const long items = long(batch) * heads_kv * pl.ns;
+  int m = SINK_LAUNCH_SPLIT;
+  long n = items;
+  if (pl.tc) {
+    m = SINK_LAUNCH_TENSOR;
+    n = items < num_sms ? items : num_sms;
+  } else if (pl.cluster) {
+    m = SINK_LAUNCH_CLUSTER;
+  }
+  if (op == SINK_OP_APPEND) n = 0;
+  if (mode) *mode = m;
+  if (ctas) *ctas = int32_t(n);
   return SINK_OK;
 }
 

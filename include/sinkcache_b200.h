@@ -18,9 +18,10 @@
  *     comes from sink_workspace_bytes().  Every launch is CUDA-graph capturable.
  *   - Return value: 0 on success, a negative SINK_E* code for a rejected argument, or a
  *     positive cudaError_t from the launch.  sink_strerror() describes any code.
- *   - The device workspace starts with a 32-bit status word.  A kernel whose bounded wait
- *     for a bulk copy runs out sets a SINK_STATUS_* bit there instead of hanging;
- *     sink_read_status() returns and clears it.
+ *   - The device workspace starts with a 256-byte header holding a 32-bit status word, zero
+ *     when the workspace is first used.  A kernel whose bounded wait for a bulk copy runs
+ *     out sets a SINK_STATUS_* bit there instead of hanging; sink_read_status() returns and
+ *     clears it.
  */
 #ifndef SINKCACHE_B200_H
 #define SINKCACHE_B200_H
@@ -116,6 +117,22 @@ int32_t sink_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
                   int32_t drop, int32_t num_sms, int32_t* splits, int32_t* rows_per_split,
                   int32_t* chunk_rows, int32_t* stages, int32_t* smem_bytes,
                   int32_t* cluster_ctas);
+
+/* launch modes reported by sink_plan_launch() */
+#define SINK_LAUNCH_SPLIT 0      /* one CTA per split; halo pre-pass and combine launches as needed */
+#define SINK_LAUNCH_CLUSTER 1    /* every split of a pair in one thread-block cluster: one launch */
+#define SINK_LAUNCH_TENSOR 2     /* the tensor-core attention kernel (16-bit K, head_dim 128) */
+
+/*
+ * How the plan of sink_plan() is launched (for tests and profiling): *mode is one of
+ * SINK_LAUNCH_*, *ctas the CTAs of the main kernel's grid (the tensor-core launch is
+ * persistent: one CTA per SM at most).  Same arguments as sink_plan; pure host arithmetic.
+ * No counterpart in the reference.  Returns 0 or SINK_E*.
+ */
+int32_t sink_plan_launch(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q,
+                         int32_t head_dim, int32_t k_dtype, int32_t v_dtype, int32_t rows,
+                         int32_t n_sink, int32_t window, int32_t drop, int32_t num_sms,
+                         int32_t* mode, int32_t* ctas);
 
 /*
  * Append: kv[:, :, row:row+n] = (k_new, v_new)  (k converted to k_dtype exactly, or rounded

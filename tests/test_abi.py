@@ -48,6 +48,7 @@ def test_workspace_and_plan_are_host_arithmetic(built_lib):
     assert p["splits"] == 74 and p["rows_per_split"] == 14 * 32
     p = _lib.plan(_lib.OP_FUSED_STEP, 1, 8, 16, 128, f32, bf16, 32769, 4, 32764, 1, 148)
     assert p["splits"] * 8 == 296 and p["rows_per_split"] == 28 * 32
+    assert p["launch"] == _lib.LAUNCH_SPLIT and p["ctas"] == 296
     ws = _lib.workspace_bytes(_lib.OP_FUSED_STEP, 8, 8, 16, 128, f32, bf16, 32769, 4, 32764, 1, 148)
     assert ws >= 256
     # unsupported shapes are rejected with 0 bytes / an error code
@@ -86,13 +87,13 @@ def test_plan_covers_rows_exactly(op, rows, n_sink, window, drop, batch, kdt):
         assert ns <= -(-(-(-total // t)) // (2 if t == 128 else 8))
 
 
-@pytest.mark.parametrize("batch,slots,ns,clustered", [
-    (1, 256, 9, True), (1, 1024, 11, True), (2, 2047, 16, True), (7, 4096, 5, True), (8, 1024, 4, True),
-    (2, 4096, 17, False), (4, 4096, 9, False), (2, 8192, 18, False), (4, 8192, 9, False),
-    (1, 4096, 33, False), (64, 256, 1, False), (1, 32768, 37, False), (8, 4096, 9, False),
-    (64, 32768, 33, False),
+@pytest.mark.parametrize("batch,slots,ns,mode", [
+    (1, 256, 9, "cluster"), (1, 1024, 11, "cluster"), (2, 2047, 16, "cluster"), (7, 4096, 5, "cluster"),
+    (8, 1024, 4, "cluster"), (2, 4096, 17, "split"), (4, 4096, 9, "split"), (2, 8192, 18, "split"),
+    (4, 8192, 9, "split"), (1, 4096, 33, "split"), (64, 256, 1, "split"), (1, 32768, 37, "split"),
+    (8, 4096, 9, "split"), (64, 32768, 33, "split"), (1, 16384, 37, "split"),
 ])
-def test_plan_clusters_small_steps(batch, slots, ns, clustered, built_lib):
+def test_plan_clusters_small_steps(batch, slots, ns, mode, built_lib):
     """Fused steps whose CTAs fit one wave with at most 16 splits per pair (or 16 splits
     that add at most 4 chunks per split) run as one clustered launch: no halo or partials
     workspace.  Clusters of more than 8 CTAs only for splits of at most 4 chunks.  Several
@@ -100,7 +101,9 @@ def test_plan_clusters_small_steps(batch, slots, ns, clustered, built_lib):
     f32, bf16 = torch.float32, torch.bfloat16
     args = (_lib.OP_FUSED_STEP, batch, 8, 16, 128, f32, bf16, slots + 1, 4, slots - 4, 1, 148)
     p = _lib.plan(*args)
-    assert p["splits"] == ns and p["cluster_ctas"] == (ns if clustered else 1)
+    clustered = mode == "cluster"
+    want = {"split": _lib.LAUNCH_SPLIT, "cluster": _lib.LAUNCH_CLUSTER}[mode]
+    assert p["splits"] == ns and p["cluster_ctas"] == (ns if clustered else 1) and p["launch"] == want
     ws = _lib.workspace_bytes(*args)
     assert (ws == 256) == (clustered or ns == 1)  # the status word alone
     # a shift of more than 4 rows, or 16-bit K attention on the tensor cores, is never clustered

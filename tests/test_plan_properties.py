@@ -54,6 +54,14 @@ def test_plan_invariants(built_lib, args):
         assert ns <= 16 and pairs * ns <= slots and drop <= 4
         if ns > 8:
             assert rps // t <= 4
+    # the launch mode agrees with the plan: clusters of ns CTAs, or the tensor-core kernel's
+    # persistent grid (one CTA per SM at most), or one CTA per split
+    if ctas > 1:
+        assert p["launch"] == _lib.LAUNCH_CLUSTER and p["ctas"] == pairs * ns
+    elif tensor_cores:
+        assert p["launch"] == _lib.LAUNCH_TENSOR and p["ctas"] == min(pairs * ns, sms)
+    else:
+        assert p["launch"] == _lib.LAUNCH_SPLIT and p["ctas"] == pairs * ns
     ws = _lib.workspace_bytes(*args)
     attends = op != _lib.OP_EVICT
     if ctas > 1 or ns == 1:
