@@ -481,6 +481,33 @@ def time_graph(bench: OpBench, steps: int, flush: torch.Tensor | None) -> float:
     return total / steps
 
 
+def graph_floor(device: torch.device, flush: torch.Tensor, steps: int = 50) -> float:
+    """µs of one CUDA-graph replay of a one-element kernel, timed like the sweep (CUDA events
+    around the replay, L2 overwritten before each): the fixed cost inside every sweep number."""
+    x = torch.zeros(1, device=device)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        x.add_(1)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        x.add_(1)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    total = 0.0
+    for i in range(steps):
+        flush_l2(flush, i)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        graph.replay()
+        end.record()
+        end.synchronize()
+        total += start.elapsed_time(end)
+    return round(total / steps * 1e3, 2)
+
+
 def sweep(device: torch.device, flush: torch.Tensor, cls=None, alg=None) -> dict:
     """µs per layer-step and GB/s over the op-bench grid (slots x streams), 1 GPU, from
     CUDA-graph replays (L2 flushed between replays when the state is smaller than 2x L2)."""
@@ -944,6 +971,7 @@ def main():
         if not args.no_sweep:
             flush = torch.empty(512 * 2 ** 20, dtype=torch.uint8, device=device)
             extra["sweep"] = sweep(device, flush, kind["cls"], alg)
+            extra["sweep_graph_floor_us"] = graph_floor(device, flush)
             del flush
             torch.cuda.empty_cache()
         if not args.no_cpu:
