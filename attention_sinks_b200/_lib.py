@@ -24,7 +24,7 @@ EXPORTED_SYMBOLS = (
     "sink_abi_version", "sink_strerror", "sink_workspace_bytes", "sink_plan", "sink_append",
     "sink_evict_rerotate", "sink_decode_attention", "sink_fused_decode_step", "sink_read_status",
     "sink_decode_attention_noalloc", "sink_v2_place", "sink_v2_decode_step", "sink_prepare_device",
-    "sink_debug_fail_next_wait", "sink_plan_launch",
+    "sink_debug_fail_next_wait", "sink_plan_launch", "sink_evict_rerotate_keycopy",
 )
 LAUNCH_SPLIT, LAUNCH_CLUSTER, LAUNCH_TENSOR = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 16 << 20
@@ -69,6 +69,7 @@ def _declare(lib):
         "sink_plan_launch": (i32, [i32] * 12 + [pi32] * 2),
         "sink_append": (i32, [pkv, prows, prows, i32, vp]),
         "sink_evict_rerotate": (i32, [pkv, i32, i32, i32, fp, fp, i32, vp, sz, vp]),
+        "sink_evict_rerotate_keycopy": (i32, [pkv, i32, i32, i32, fp, fp, i32, prows, vp, sz, vp]),
         "sink_decode_attention": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
         "sink_fused_decode_step": (i32, [pkv, prows, prows, prows, i32, i32, i32, i32, fp, fp, i32,
                                          ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
@@ -275,6 +276,24 @@ def evict_rerotate(kbuf: torch.Tensor, vbuf: torch.Tensor, n_sink: int, window: 
                                    1 if rotate else 0, buf.data_ptr(), buf.numel(),
                                    stream_handle(kbuf.device))
     _check(rc, "sink_evict_rerotate")
+
+
+def evict_rerotate_keycopy(kbuf: torch.Tensor, vbuf: torch.Tensor, n_sink: int, window: int, drop: int,
+                           cos: torch.Tensor | None, sin: torch.Tensor | None, k_copy: torch.Tensor,
+                           ws: Workspace) -> None:
+    """evict_rerotate (nothing moves when drop == 0) that also writes the window rows' final
+    keys, rounded to the value dtype, into k_copy rows [n_sink, n_sink + window)."""
+    kv = kv_desc(kbuf, vbuf)
+    b, h, _, d = kbuf.shape
+    need = workspace_bytes(OP_EVICT, b, h, h, d, kbuf.dtype, vbuf.dtype, 0, n_sink, window, drop,
+                           sm_count(kbuf.device))
+    buf = ws.get(need, kbuf.device)
+    rotate = cos is not None and drop > 0
+    rc = lib().sink_evict_rerotate_keycopy(ctypes.byref(kv), n_sink, window, drop,
+                                           cos.data_ptr() if rotate else None, sin.data_ptr() if rotate else None,
+                                           1 if rotate else 0, ctypes.byref(rows_desc(k_copy)), buf.data_ptr(),
+                                           buf.numel(), stream_handle(kbuf.device))
+    _check(rc, "sink_evict_rerotate_keycopy")
 
 
 def mask_arg(mask: torch.Tensor | None, batch: int, rows: int) -> tuple[int | None, int, torch.Tensor | None]:

@@ -44,6 +44,21 @@ def pending_layer(key: torch.Tensor) -> "SinkLayer | None":
     return layer
 
 
+class KeyCopy:
+    """Device buffer for the model-dtype key copy a multi-token (or unfused) step hands to
+    attention, grown on demand and reused.  A cache's layers share one: each layer's copy is
+    consumed by its attention before the next layer's update overwrites it."""
+
+    def __init__(self):
+        self.buf = None
+
+    def view(self, b: int, h: int, rows: int, d: int, dtype: torch.dtype, device) -> torch.Tensor:
+        n = b * h * rows * d
+        if self.buf is None or self.buf.numel() < n or self.buf.dtype != dtype or self.buf.device != device:
+            self.buf = torch.empty(n, dtype=dtype, device=device)
+        return self.buf[:n].view(b, h, rows, d)
+
+
 class SinkLayer(CacheLayerMixin):
     """One layer's cache: `n_sink` sink tokens + a rolling window of `window` tokens
     (src/sinkcache/cache.py:54-198)."""
@@ -53,7 +68,8 @@ class SinkLayer(CacheLayerMixin):
 
     def __init__(self, n_sink: int, window: int, inv_freq: torch.Tensor, rerotate_keys: bool = True,
                  use_triton: bool | None = None, key_dtype: torch.dtype | None = None,
-                 fused: bool = False, workspace: "_lib.Workspace | None" = None):
+                 fused: bool = False, workspace: "_lib.Workspace | None" = None,
+                 key_copy: "KeyCopy | None" = None):
         super().__init__()
         if n_sink < 0 or window < 1:
             raise ValueError(f"need n_sink >= 0 and window >= 1, got {n_sink}, {window}")
@@ -74,6 +90,7 @@ class SinkLayer(CacheLayerMixin):
         self._kstore = self._vstore = None  # row storage the buffers view (see _alloc)
         self._pending = None        # (drop, k, v, append_row) of a deferred one-token step
         self._ws = workspace if workspace is not None else _lib.Workspace()
+        self._key_copy = key_copy if key_copy is not None else KeyCopy()
 
     # ------------------------------------------------------------------ storage
 
@@ -89,6 +106,9 @@ class SinkLayer(CacheLayerMixin):
         self._alloc(key_states, self.capacity + 1)
         self._rotation(1)  # the steady-state shift; built now so a graph capture never builds it
         self._size_workspace(key_states)
+        if self.key_dtype != self.dtype:  # the steady step's key copy, before any capture
+            b, h, _, d = key_states.shape
+            self._key_copy.view(b, h, self.capacity + 1, d, self.dtype, self.device)
         self.is_initialized = True
 
     def _alloc(self, like, slots):
@@ -141,17 +161,21 @@ class SinkLayer(CacheLayerMixin):
             self._rot[delta] = (cos.to(self.device), sin.to(self.device))
         return self._rot[delta]
 
-    def _evict(self, kbuf, vbuf, drop):
+    def _evict(self, kbuf, vbuf, drop, key_copy=None):
         cos, sin = self._rotation(drop) if self.rerotate_keys else (None, None)
-        _lib.evict_rerotate(kbuf, vbuf, self.n_sink, self.window, drop, cos, sin, self._ws)
+        if key_copy is None:
+            _lib.evict_rerotate(kbuf, vbuf, self.n_sink, self.window, drop, cos, sin, self._ws)
+        else:
+            _lib.evict_rerotate_keycopy(kbuf, vbuf, self.n_sink, self.window, drop, cos, sin, key_copy, self._ws)
 
-    def _evict_pending(self):
+    def _evict_pending(self, key_copy=None):
         """Shift the window left by the pending `drop` rows, re-rotating keys by -drop, in
-        place (cache.py:129-147)."""
+        place (cache.py:129-147).  With `key_copy`, the same pass writes the window rows'
+        keys in the model dtype into it."""
         drop = self.length - self.capacity
         if drop <= 0:
             return
-        self._evict(self._kbuf, self._vbuf, drop)
+        self._evict(self._kbuf, self._vbuf, drop, key_copy)
         self.length = self.capacity
         self.tokens_evicted += drop
         if self._kbuf.shape[-2] > self.capacity + 1:  # a long chunk grew the buffer: shrink back
@@ -176,18 +200,36 @@ class SinkLayer(CacheLayerMixin):
             self.tokens_evicted += drop
             self.keys, self.values = self._kbuf[:, :, :self.length], self._vbuf[:, :, :self.length]
             return self.keys, self.values
-        self._evict_pending()
-        end = self.length + q
+        copy_keys = self.key_dtype != self.dtype
+        # The keys attention gets are the model-dtype copy of the buffer (cache.py:163).  Its
+        # window rows come out of the eviction kernel's pass (no separate read of the float32
+        # keys); the sink rows and the new rows are copied here.
+        b, h, _, d = key_states.shape
+        end = min(self.length, self.capacity) + q
+        kc = self._key_copy.view(b, h, end, d, self.dtype, self.device) if copy_keys else None
+        evicting = self.length > self.capacity
+        self._evict_pending(kc)
+        if copy_keys and not evicting and self.length > self.n_sink:  # nothing moved: convert
+            _lib.evict_rerotate_keycopy(self._kbuf, self._vbuf, self.n_sink, self.length - self.n_sink, 0, None,
+                                        None, kc, self._ws)
+        start = self.length
+        end = start + q
         if end > self._kbuf.shape[-2]:
             self._alloc(key_states, end)
-        _lib.append(self._kbuf, self._vbuf, key_states, value_states, self.length)
+        _lib.append(self._kbuf, self._vbuf, key_states, value_states, start)
         self.length = end
         self.tokens_seen += q
-        keys = self._kbuf[:, :, :end]
-        if not self.fused:
-            keys = keys.to(self.dtype)  # what a stock attention backend expects (cache.py:163)
-        self.keys, self.values = keys, self._vbuf[:, :, :end]
-        return self.keys, self.values
+        if copy_keys:
+            s = min(self.n_sink, start)
+            if s:
+                kc[:, :, :s].copy_(self._kbuf[:, :, :s])
+            kc[:, :, start:end].copy_(key_states)
+            keys = kc
+        else:
+            keys = self._kbuf[:, :, :end]
+        # the layer keeps views of its own buffers; the copy is valid until the next layer's update
+        self.keys, self.values = self._kbuf[:, :, :end], self._vbuf[:, :, :end]
+        return keys, self.values
 
     def run_pending(self, query: torch.Tensor, scale: float, mask: torch.Tensor | None = None) -> torch.Tensor:
         """Run the deferred step fused with its attention; returns [B, 1, Hq, D].  `mask`:
@@ -283,10 +325,12 @@ class SinkCache(Cache):
     def __init__(self, n_sink: int, window: int, inv_freq: torch.Tensor, num_layers: int,
                  rerotate_keys: bool = True, use_triton: bool | None = None,
                  key_dtype: torch.dtype | None = torch.float32, fused: bool = False):
-        # one workspace for all layers: they run one after another on one stream
+        # one workspace and one key copy for all layers: they run one after another on one stream
         self.workspace = _lib.Workspace()
+        self.key_copy = KeyCopy()
         layers = [SinkLayer(n_sink, window, inv_freq, rerotate_keys, use_triton, key_dtype,
-                            fused=fused, workspace=self.workspace) for _ in range(num_layers)]
+                            fused=fused, workspace=self.workspace, key_copy=self.key_copy)
+                  for _ in range(num_layers)]
         super().__init__(layers=layers)
         self.n_sink, self.window = n_sink, window
 

@@ -107,9 +107,10 @@ struct StreamLanes {
 
   // One chunk of rows [x, xe) staged at sk / sv (row t of the chunk at sk + t * D):
   // window rows are re-rotated in place in shared memory, then (ATTEND) scored and folded
-  // into the online softmax.  `mrow`: optional per-row mask of this pair.
+  // into the online softmax.  `mrow`: optional per-row mask of this pair.  `mirror`
+  // (optional): this pair's key copy in the value type; row r of it gets row r's key.
   __device__ __forceinline__ void chunk(KT* sk, const VT* sv, int x, int xe, const StreamArgs& A,
-                                        const uint8_t* mrow) {
+                                        const uint8_t* mrow, VT* mirror = nullptr) {
     const int wend = A.n_sink + A.window;
     float sc[NG][STEPS];
 #pragma unroll
@@ -133,6 +134,11 @@ struct StreamLanes {
         }
         Elem<KT>::store4(krow + 4 * li, lo);
         Elem<KT>::store4(krow + D / 2 + 4 * li, hi);
+      }
+      if (mirror != nullptr && valid) {  // the row's final key, in the value type
+        VT* mrow_k = mirror + size_t(r) * D;
+        Elem<VT>::store4(mrow_k + 4 * li, lo);
+        Elem<VT>::store4(mrow_k + D / 2 + 4 * li, hi);
       }
       if constexpr (ATTEND) {
         const bool seen = valid && (mrow == nullptr || mrow[r] != 0);

@@ -71,6 +71,11 @@ struct StreamArgs {
   // Failure-detection test hook, -1 when off: every CTA leaves its chunk `skip_chunk`
   // unissued (no copy, no arrival), so the wait for it runs out with nothing in flight.
   int skip_chunk;
+  // Optional key copy in the value type (chunk steps): every output row r the launch handles
+  // is also written, rounded to the value type, to kmirror row r (element strides of batch
+  // and head km_sb / km_sh, rows contiguous).  NULL: none.
+  char* kmirror;
+  int64_t km_sb, km_sh;
 };
 
 // Rows [a, e) of split j.

@@ -135,6 +135,7 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
   const unsigned char* hv =
       clustered ? nullptr : reinterpret_cast<const unsigned char*>(A.halo_v) + halo_row0 * VROW;
   const int nchunks = (e - a + T - 1) / T;
+  VT* kmir = A.kmirror != nullptr ? reinterpret_cast<VT*>(A.kmirror) + b * A.km_sb + h * A.km_sh : nullptr;
 
   if (tid == 0) {
 #pragma unroll
@@ -215,7 +216,7 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
         __syncthreads();
       }
     }
-    if (!failed) L.chunk(sk, sv, x, xe, A, mrow);
+    if (!failed) L.chunk(sk, sv, x, xe, A, mrow, kmir);
     int st_lo, st_hi;
     store_range(A, x, xe, st_lo, st_hi);
     fence_proxy_async_smem();
@@ -327,12 +328,15 @@ struct HaloBytes {
   int krow, vrow;                  // bytes per row (multiples of 16)
 };
 
-// Boundaries (splits) whose halo one CTA of sink_halo_kernel copies.
-constexpr int kHaloSplitsPerCta = 8;
+// 16-byte words of halo rows each thread of sink_halo_kernel copies per round (all loads of a
+// round are issued before its stores).
+constexpr int kHaloWordsPerThread = 4;
 
 // Copies the halo rows of every split but the last into the workspace (pre-pass of an
-// in-place shift that spans several splits).  Grid: (ceil((ns - 1) / kHaloSplitsPerCta),
-// batch * heads_kv).
+// in-place shift that spans several splits).  Grid: (ceil(words / (kThreads *
+// kHaloWordsPerThread)), batch * heads_kv), words = (ns - 1) * halo_rows * (K + V row words).
+// A round of a thread covers words i, i + kThreads, ... of its CTA's tile, so every load
+// instruction is coalesced and a round's loads are all in flight before the first store.
 __global__ void __launch_bounds__(kThreads) sink_halo_kernel(const __grid_constant__ StreamArgs A,
                                                              const HaloBytes H) {
   allow_dependents();  // the stream kernel may launch; it waits for this grid to complete
@@ -341,27 +345,38 @@ __global__ void __launch_bounds__(kThreads) sink_halo_kernel(const __grid_consta
   const int kv4 = H.krow / (int)sizeof(uint4), vv4 = H.vrow / (int)sizeof(uint4);
   const uint4* kbase = reinterpret_cast<const uint4*>(A.kbuf + b * H.k_sb + h * H.k_sh);
   const uint4* vbase = reinterpret_cast<const uint4*>(A.vbuf + b * H.v_sb + h * H.v_sh);
-  const int j0 = blockIdx.x * kHaloSplitsPerCta;
-  const int j1 = imin(j0 + kHaloSplitsPerCta, A.ns - 1);
-  // One flat index space over (split, halo row, 16-byte word), K words then V words, so that
-  // every load of the CTA is independent (a latency-bound copy of a few rows per split).
+  // one flat index space over (split, halo row, 16-byte word), K words then V words
+  const int nb = A.ns - 1;
   const int kper = A.halo_rows * kv4, vper = A.halo_rows * vv4;
-  const int nk = (j1 - j0) * kper, total = nk + (j1 - j0) * vper;
-  for (int i = threadIdx.x; i < total; i += kThreads) {
-    const bool isk = i < nk;
-    const int per = isk ? kper : vper, w4 = isk ? kv4 : vv4;
-    const int li = isk ? i : i - nk;
-    const int j = j0 + li / per, r = (li % per) / w4, c = li % w4;
-    int a, e;
-    split_rows(A.row_begin, A.row_end, A.rows_per_split, j, a, e);
-    int hlo, hhi;
-    halo_range(A.n_sink, A.window, A.drop, A.written_end, false, a, e, hlo, hhi);
-    if (hlo + r >= hhi) continue;
-    const size_t dst = ((size_t(p) * A.ns + j) * A.halo_rows + r) * w4 + c;
-    if (isk)
-      reinterpret_cast<uint4*>(A.halo_k)[dst] = kbase[size_t(hlo + r) * kv4 + c];
-    else
-      reinterpret_cast<uint4*>(A.halo_v)[dst] = vbase[size_t(hlo + r) * vv4 + c];
+  const int nk = nb * kper, total = nk + nb * vper;
+  constexpr int U = kHaloWordsPerThread;
+  for (int tile = blockIdx.x * (kThreads * U); tile < total; tile += gridDim.x * (kThreads * U)) {
+    uint4 w[U];
+    size_t dst[U];
+    int kind[U];  // 0: nothing, 1: K word, 2: V word
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = tile + u * kThreads + threadIdx.x;
+      kind[u] = 0;
+      if (i >= total) continue;
+      const bool isk = i < nk;
+      const int per = isk ? kper : vper, w4 = isk ? kv4 : vv4;
+      const int li = isk ? i : i - nk;
+      const int j = li / per, r = (li % per) / w4, c = li % w4;
+      int a, e;
+      split_rows(A.row_begin, A.row_end, A.rows_per_split, j, a, e);
+      int hlo, hhi;
+      halo_range(A.n_sink, A.window, A.drop, A.written_end, false, a, e, hlo, hhi);
+      if (hlo + r >= hhi) continue;
+      dst[u] = ((size_t(p) * A.ns + j) * A.halo_rows + r) * w4 + c;
+      w[u] = isk ? kbase[size_t(hlo + r) * kv4 + c] : vbase[size_t(hlo + r) * vv4 + c];
+      kind[u] = isk ? 1 : 2;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (kind[u] == 1) reinterpret_cast<uint4*>(A.halo_k)[dst[u]] = w[u];
+      else if (kind[u] == 2) reinterpret_cast<uint4*>(A.halo_v)[dst[u]] = w[u];
+    }
   }
 }
 

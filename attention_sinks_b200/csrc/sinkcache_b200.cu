@@ -177,6 +177,25 @@ void choose_cluster(int pairs, int rows, int T, int slots, int drop, Plan& pl) {
   pl.cluster = ns > 1;
 }
 
+// An in-place shift by `drop` rows copies, per split boundary, the halo rows the next split
+// would overwrite first (min(drop, rows per split) rows): with splits not much longer than
+// the shift, most of the window would make that round trip through the workspace (a 512-row
+// shift at 4,096 slots x 8 streams took 483 us against 87 us for 16 rows).  So a shifting
+// plan keeps its splits at least kHaloSplitRatio times the shift, in fewer, longer splits.
+constexpr long kHaloSplitRatio = 3;
+
+void limit_halo(int rows, int drop, Plan& pl) {
+  const long want = kHaloSplitRatio * long(drop);
+  if (pl.ns < 2 || pl.rows_per_split >= want) return;
+  const long tiles = (rows + pl.T - 1) / pl.T;
+  long tps = (want + pl.T - 1) / pl.T;
+  long ns = tiles / tps;  // every split (the last one too) at least `want` rows
+  if (ns < 1) ns = 1;
+  tps = (tiles + ns - 1) / ns;  // even the splits out
+  pl.ns = int((tiles + tps - 1) / tps);
+  pl.rows_per_split = int(tps) * pl.T;
+}
+
 int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, int32_t D,
                   int32_t kdt, int32_t vdt, int32_t rows, int32_t n_sink, int32_t window,
                   int32_t drop, int32_t num_sms, Plan& pl) {
@@ -206,6 +225,7 @@ int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
     choose_splits(pairs, nrows, pl.T, num_sms, kTcTargetItemsPerCta, kTcMinItemChunks, false, pl);
   else {
     choose_splits(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, kTargetWaves, kMinItemChunks, true, pl);
+    if (drop > 0 && (op == SINK_OP_EVICT || op == SINK_OP_FUSED_STEP)) limit_halo(nrows, drop, pl);
     choose_cluster(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, drop, pl);
   }
   size_t off = 256;  // status word
@@ -423,8 +443,10 @@ int32_t launch_halo(const sink_kv_buffers_t* kv, const StreamArgs& A, const Plan
   H.v_sh = kv->v_stride_h * vs;
   H.krow = kv->head_dim * ks;
   H.vrow = kv->head_dim * vs;
-  const int cx = (pl.ns - 1 + kHaloSplitsPerCta - 1) / kHaloSplitsPerCta;
-  sink_halo_kernel<<<dim3(cx, pairs), kThreads, 0, st>>>(A, H);
+  const long words = long(pl.ns - 1) * pl.halo_rows * ((H.krow + H.vrow) / 16);
+  long cx = (words + kThreads * kHaloWordsPerThread - 1) / (kThreads * kHaloWordsPerThread);
+  if (cx > 65535) cx = 65535;
+  sink_halo_kernel<<<dim3(unsigned(cx), pairs), kThreads, 0, st>>>(A, H);
   return cudaGetLastError();
 }
 
@@ -995,16 +1017,27 @@ int32_t sink_append(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
   return launch_append_t<float, float>(kv, k_new, v_new, row, st);
 }
 
-int32_t sink_evict_rerotate(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t window,
-                            int32_t drop, const float* cos_tab, const float* sin_tab,
-                            int32_t rotate, void* workspace, size_t workspace_bytes,
-                            void* stream) {
+}  // extern "C"
+
+namespace {
+
+// sink_evict_rerotate, and with `kc` the variant that also writes every window row's final
+// key, in the value type, into kc (then drop == 0 launches too: a pure conversion).
+int32_t evict_launch(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t window, int32_t drop,
+                     const float* cos_tab, const float* sin_tab, int32_t rotate,
+                     const sink_rows_t* kc, void* workspace, size_t workspace_bytes,
+                     void* stream) {
   int32_t rc = check_kv(kv);
   if (rc) return rc;
   if (n_sink < 0 || window < 1 || drop < 0) return SINK_EINVAL;
   if (int64_t(n_sink) + window + drop > kv->slots) return SINK_EINVAL;
-  if (drop == 0) return SINK_OK;
-  if (rotate && (!cos_tab || !sin_tab)) return SINK_EINVAL;
+  if (kc) {
+    if ((rc = check_rows(kc, kv->v_dtype, kv->batch, kv->heads_kv, kc->n))) return rc;
+    if (kc->n < n_sink + window || kc->stride_t != kv->head_dim) return SINK_ELAYOUT;
+    if (!rows_aligned16(kc, elem_size(kv->v_dtype))) return SINK_ELAYOUT;
+  }
+  if (drop == 0 && !kc) return SINK_OK;
+  if (drop > 0 && rotate && (!cos_tab || !sin_tab)) return SINK_EINVAL;
   int dev = 0;
   const int sms = device_sms(&dev);
   if (sms <= 0) return SINK_EDEVICE;
@@ -1024,10 +1057,36 @@ int32_t sink_evict_rerotate(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t
   A.row_begin = n_sink;
   A.row_end = n_sink + window;
   A.written_end = n_sink + window;
+  if (kc) {
+    A.kmirror = static_cast<char*>(kc->data);
+    A.km_sb = kc->stride_b;
+    A.km_sh = kc->stride_h;
+  }
   const int pairs = kv->batch * kv->heads_kv;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((rc = launch_halo(kv, A, pl, pairs, st))) return rc;
   return dispatch_stream<false>(kv->k_dtype, kv->v_dtype, kv->head_dim, 1, A, pl, pairs, st, dev);
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t sink_evict_rerotate(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t window,
+                            int32_t drop, const float* cos_tab, const float* sin_tab,
+                            int32_t rotate, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  return evict_launch(kv, n_sink, window, drop, cos_tab, sin_tab, rotate, nullptr, workspace,
+                      workspace_bytes, stream);
+}
+
+int32_t sink_evict_rerotate_keycopy(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t window,
+                                    int32_t drop, const float* cos_tab, const float* sin_tab,
+                                    int32_t rotate, const sink_rows_t* k_copy, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  if (!k_copy) return SINK_EINVAL;
+  return evict_launch(kv, n_sink, window, drop, cos_tab, sin_tab, rotate, k_copy, workspace,
+                      workspace_bytes, stream);
 }
 
 int32_t sink_decode_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows,

@@ -160,6 +160,21 @@ int32_t sink_evict_rerotate(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t
                             void* stream);
 
 /*
+ * sink_evict_rerotate that also writes every window row's final key, rounded to the value
+ * type, into k_copy rows [n_sink, n_sink + window) (k_copy: [batch, heads_kv, >= n_sink +
+ * window, head_dim] in v_dtype, rows contiguous and 16-byte aligned) -- in the same pass over
+ * the cache.  With drop == 0 nothing moves and the launch only writes the copy.
+ * Replaces, for a multi-token step, the model-dtype key copy SinkLayer.update returns
+ * (`self._kbuf[:, :, :end].to(self.dtype)`, cache.py:163) for the window rows: the copy no
+ * longer costs a separate read of the float32 keys.  The caller copies the sink rows and the
+ * appended rows itself.
+ */
+int32_t sink_evict_rerotate_keycopy(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t window,
+                                    int32_t drop, const float* cos_tab, const float* sin_tab,
+                                    int32_t rotate, const sink_rows_t* k_copy, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
+/*
  * Decode attention for one query token per sequence over the first `rows` cache rows:
  *   out[b, 0, hq, :] = softmax(q[b, hq] . K[b, hq / G, :rows]^T * scale) @ V[b, hq / G, :rows]
  * with G = q->heads / heads_kv (grouped-query attention, HF repeat_kv head order).

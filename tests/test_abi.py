@@ -66,7 +66,8 @@ def test_workspace_and_plan_are_host_arithmetic(built_lib):
 @pytest.mark.parametrize("op,rows,n_sink,window,drop", [
     (_lib.OP_EVICT, 0, 4, 60, 1), (_lib.OP_EVICT, 0, 4, 32764, 1), (_lib.OP_EVICT, 0, 2, 7, 200),
     (_lib.OP_ATTEND, 1, 0, 1, 0), (_lib.OP_ATTEND, 4097, 0, 1, 0), (_lib.OP_FUSED_STEP, 1025, 4, 1020, 1),
-    (_lib.OP_FUSED_STEP, 257, 4, 252, 0),
+    (_lib.OP_FUSED_STEP, 257, 4, 252, 0), (_lib.OP_EVICT, 0, 4, 4092, 512), (_lib.OP_EVICT, 0, 4, 32764, 512),
+    (_lib.OP_FUSED_STEP, 4097, 4, 4092, 128),
 ])
 @pytest.mark.parametrize("batch", [1, 8, 64])
 @pytest.mark.parametrize("kdt", [torch.float32, torch.bfloat16], ids=["k32", "k16"])
@@ -80,7 +81,11 @@ def test_plan_covers_rows_exactly(op, rows, n_sink, window, drop, batch, kdt):
         assert p["chunk_rows"] == 128 and p["stages"] == 3
     total = window if op == _lib.OP_EVICT else rows
     ns, rps, t = p["splits"], p["rows_per_split"], p["chunk_rows"]
-    assert rps % t == 0 and 1 <= ns <= 256 and rps <= 32 * t
+    # items of at most 32 chunks, or, for a shift, 3 to 6 shifts long (short splits would
+    # send most of the window through the halo copy)
+    assert rps % t == 0 and 1 <= ns <= 256 and rps <= max(32 * t, 6 * drop + 2 * t)
+    if drop > 0 and ns > 1 and op != _lib.OP_ATTEND:
+        assert rps >= 3 * drop
     assert (ns - 1) * rps < total <= ns * rps
     slots = 148 * (233472 // (p["smem_bytes"] + 1024))  # CTA slots: SMs x CTAs per SM
     if batch * 8 * ns > slots:  # several waves: no more splits than items of 8 (tensor cores: 2) chunks give

@@ -280,3 +280,35 @@ def test_fused_step_with_boolean_mask(built_lib):
     assert digest(kbuf.cpu()) == digest(want.kbuf)
     torch.testing.assert_close(vbuf.cpu(), want.vbuf, rtol=0, atol=0)
     torch.testing.assert_close(out.float().cpu(), want_out, rtol=2e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("batch,heads,n_sink,window,drop,d", [
+    (1, 8, 4, 1020, 1, 128), (2, 8, 4, 4092, 16, 128), (1, 8, 4, 32764, 16, 128),
+    (3, 8, 0, 300, 37, 64), (2, 8, 4, 1020, 0, 128), (1, 8, 2, 500, 3, 256),
+])
+def test_eviction_key_copy_matches_reference(batch, heads, n_sink, window, drop, d, built_lib):
+    """The eviction pass also writes the window rows' keys in the model dtype (what a chunk
+    step hands to SDPA, cache.py:163): bit for bit the bf16 rounding of the reference's
+    re-rotated fp32 keys; drop 0 converts without moving anything."""
+    g = torch.Generator().manual_seed(batch * 100 + window + drop)
+    inv = cases.inv_freq(d, 1e6)
+    rows = n_sink + window + drop
+    k = torch.randn(batch, heads, rows + 2, d, generator=g) * 10
+    v = torch.randn(batch, heads, rows + 2, d, generator=g).bfloat16()
+    want = oracle.OracleSinkLayer(n_sink, window, inv, key_dtype=torch.float32)
+    want.dtype = torch.bfloat16
+    want.kbuf, want.vbuf, want.length = k.clone(), v.clone(), rows
+    want.evict_pending()
+    kbuf, vbuf = k.to(DEV), v.to(DEV)
+    copy = torch.full((batch, heads, rows, d), float("nan"), dtype=torch.bfloat16, device=DEV)
+    cos, sin = [t.to(DEV) for t in oracle.rope_cos_sin(torch.tensor(-max(drop, 1)), inv)]
+    ws = _lib.Workspace()
+    _lib.evict_rerotate_keycopy(kbuf, vbuf, n_sink, window, drop, cos, sin, copy, ws)
+    torch.cuda.synchronize()
+    _status_clean(ws)
+    cap = n_sink + window
+    got = copy[:, :, n_sink:cap].cpu()
+    torch.testing.assert_close(got, want.kbuf[:, :, n_sink:cap].bfloat16(), rtol=0, atol=0)
+    assert torch.isnan(copy[:, :, :n_sink].float()).all()  # sink rows are the caller's
+    assert digest(kbuf[:, :, :cap].cpu()) == digest(want.kbuf[:, :, :cap])
+    torch.testing.assert_close(vbuf[:, :, :cap].cpu(), want.vbuf[:, :, :cap], rtol=0, atol=0)

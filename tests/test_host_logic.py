@@ -26,6 +26,12 @@ def fake_evict(kbuf, vbuf, n_sink, window, drop, cos, sin, ws):
     vbuf[:, :, s:s + window].copy_(new_v)
 
 
+def fake_evict_keycopy(kbuf, vbuf, n_sink, window, drop, cos, sin, k_copy, ws):
+    if drop:
+        fake_evict(kbuf, vbuf, n_sink, window, drop, cos, sin, ws)
+    k_copy[:, :, n_sink:n_sink + window].copy_(kbuf[:, :, n_sink:n_sink + window])
+
+
 def fake_append(kbuf, vbuf, k, v, row):
     kbuf[:, :, row:row + k.shape[-2]].copy_(k)
     vbuf[:, :, row:row + v.shape[-2]].copy_(v)
@@ -49,7 +55,7 @@ def fake_fused(kbuf, vbuf, k, v, q, n_sink, window, drop, append_row, cos, sin, 
 
 @pytest.fixture
 def cpu_kernels(monkeypatch):
-    calls = {"evict": 0, "append": 0, "fused": 0, "attend": 0}
+    calls = {"evict": 0, "evict_keycopy": 0, "append": 0, "fused": 0, "attend": 0}
 
     def count(name, fn):
         def wrapped(*a, **k):
@@ -61,6 +67,7 @@ def cpu_kernels(monkeypatch):
     monkeypatch.setattr(_lib, "prepare_device", lambda device: None)
     monkeypatch.setattr(_lib, "sm_count", lambda device: 148)
     monkeypatch.setattr(_lib, "evict_rerotate", count("evict", fake_evict))
+    monkeypatch.setattr(_lib, "evict_rerotate_keycopy", count("evict_keycopy", fake_evict_keycopy))
     monkeypatch.setattr(_lib, "append", count("append", fake_append))
     monkeypatch.setattr(_lib, "fused_decode_step", count("fused", fake_fused))
     monkeypatch.setattr(_lib, "decode_attention", count("attend", fake_attention))
@@ -142,6 +149,31 @@ def test_unfused_returns_model_dtype_keys(cpu_kernels):
     keys, _ = layer.update(torch.randn(1, 2, 3, 64).bfloat16(), torch.randn(1, 2, 3, 64).bfloat16())
     assert keys.dtype == torch.bfloat16  # what stock SDPA expects (cache.py:163)
     assert layer._kbuf.dtype == torch.float32
+
+
+@pytest.mark.parametrize("fused", [False, True], ids=["unfused", "fused"])
+def test_model_dtype_keys_come_from_the_eviction_pass(cpu_kernels, fused):
+    """fp32 key storage, bf16 model: every multi-token (and unfused) step returns the bf16
+    copy of the cache (cache.py:163) -- window rows written by the eviction pass itself (or
+    converted when nothing is evicted), sink and new rows copied -- bit for bit what the
+    reference returns; the layer keeps views of its own fp32 buffers."""
+    inv = 1.0 / (1e6 ** (torch.arange(0, 64, 2, dtype=torch.float32) / 64))
+    layer = SinkLayer(4, 20, inv, key_dtype=torch.float32, fused=fused)
+    want = oracle.OracleSinkLayer(4, 20, inv, key_dtype=torch.float32)
+    g = torch.Generator().manual_seed(9)
+    for n in [6, 9, 1, 1, 14, 3, 40, 2, 1, 30]:
+        k = torch.randn(1, 2, n, 64, generator=g).bfloat16()
+        v = torch.randn(1, 2, n, 64, generator=g).bfloat16()
+        keys, values = layer.update(k, v)
+        wk, wv = want.update(k, v)
+        if layer._pending is not None:  # a fused one-token step, deferred: the fp32 view
+            assert fused and n == 1 and keys.dtype == torch.float32
+            layer.materialize()
+            continue
+        assert keys.dtype == torch.bfloat16 and layer.keys.dtype == torch.float32
+        torch.testing.assert_close(keys, wk, rtol=0, atol=0)
+        torch.testing.assert_close(values, wv, rtol=0, atol=0)
+    assert cpu_kernels["evict_keycopy"] > 0
 
 
 def test_reference_argument_checks():

@@ -42,8 +42,11 @@ def test_plan_invariants(built_lib, args):
     p = _lib.plan(*args)
     ns, rps, t, ctas = p["splits"], p["rows_per_split"], p["chunk_rows"], p["cluster_ctas"]
     total = window if op == _lib.OP_EVICT else rows
-    # the splits tile the rows: no gap, no empty split, items of at most 32 chunks
-    assert ns >= 1 and rps % t == 0 and rps <= 32 * t
+    # the splits tile the rows: no gap, no empty split, items of at most 32 chunks -- longer
+    # only for a shift, whose splits stay 3 to 6 shifts long
+    assert ns >= 1 and rps % t == 0 and rps <= max(32 * t, 6 * drop + 2 * t)
+    if drop > 0 and ns > 1 and op != _lib.OP_ATTEND:
+        assert rps >= 3 * drop
     assert (ns - 1) * rps < total <= ns * rps
     pairs = batch * hkv
     tensor_cores = t == 128 and p["stages"] == 3
