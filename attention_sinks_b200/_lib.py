@@ -24,7 +24,7 @@ EXPORTED_SYMBOLS = (
     "sink_abi_version", "sink_strerror", "sink_workspace_bytes", "sink_plan", "sink_append",
     "sink_evict_rerotate", "sink_decode_attention", "sink_fused_decode_step", "sink_read_status",
     "sink_decode_attention_noalloc", "sink_v2_place", "sink_v2_decode_step", "sink_prepare_device",
-    "sink_debug_fail_next_wait", "sink_plan_launch", "sink_evict_rerotate_keycopy",
+    "sink_debug_fail_next_wait", "sink_plan_launch", "sink_evict_rerotate_keycopy", "sink_v2_gather",
 )
 LAUNCH_SPLIT, LAUNCH_CLUSTER, LAUNCH_TENSOR = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 16 << 20
@@ -78,6 +78,7 @@ def _declare(lib):
         "sink_debug_fail_next_wait": (i32, [i32, i32]),
         "sink_decode_attention_noalloc": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, vp, i64, i64, vp]),
         "sink_v2_place": (i32, [pkv, prows, prows, prows, vp, i32, prows, vp, i64, i32, i32, vp, i32, vp]),
+        "sink_v2_gather": (i32, [pkv, i32, i32, i32, i64, i64, prows, prows, prows, prows, vp]),
         "sink_v2_decode_step": (i32, [pkv, prows, prows, prows, vp, i32, vp, i32, i32, vp, i32, prows,
                                       ctypes.c_float, vp, i64, vp, i64, i64, vp, sz, vp]),
     }
@@ -427,3 +428,17 @@ def v2_decode_step(kbuf: torch.Tensor, vbuf: torch.Tensor, k: torch.Tensor, v: t
         stream_handle(kbuf.device))
     _check(rc, "sink_v2_decode_step")
     return out
+
+
+def v2_gather(kbuf: torch.Tensor, vbuf: torch.Tensor, n_sink: int, window: int, R: int, lo: int, hi: int,
+              k: torch.Tensor | None, v: torch.Tensor | None, out_k: torch.Tensor, out_v: torch.Tensor) -> None:
+    """[region, window by position, chunk] rows of a ring-buffer layer into out_k / out_v:
+    out_v rows [0, R) from the region's values (out_k's are the place kernel's), rows
+    [R, R + hi - lo) from the ring slots of positions lo .. hi - 1, then the chunk (k, v)."""
+    kv = kv_desc(kbuf, vbuf)
+    kd = ctypes.byref(rows_desc(k)) if k is not None else None
+    vd = ctypes.byref(rows_desc(v)) if v is not None else None
+    rc = lib().sink_v2_gather(ctypes.byref(kv), int(n_sink), int(window), int(R), int(lo), int(hi), kd, vd,
+                              ctypes.byref(rows_desc(out_k)), ctypes.byref(rows_desc(out_v)),
+                              stream_handle(kbuf.device))
+    _check(rc, "sink_v2_gather")

@@ -22,8 +22,8 @@ captured CUDA graph serves every later steady token.
 Device work goes through the sm_100a library: the steady one-token step is sink_v2_place
 (or, when the model uses the registered attention backend, sink_v2_decode_step: the same
 step fused with its attention); chunk steps and kept() rotate the region with
-sink_v2_place into a fresh tensor and copy the window out of the ring as at most two
-contiguous slices per tensor.
+sink_v2_place into a fresh tensor and gather the window out of the ring, in position order,
+with sink_v2_gather (one launch, 16-byte copies).
 """
 
 from __future__ import annotations
@@ -203,34 +203,34 @@ class SinkLayerV2(CacheLayerMixin):
             views.append(buf[:, :, :n - head])
         return views
 
-    def _stack_rows(self, n_region: int, parts: list[torch.Tensor],
-                    region: torch.Tensor | None) -> torch.Tensor:
-        """A new [b, h, n_region + rows of parts, d] tensor: region rows (copied from `region`,
-        or left for the caller), then the parts in order."""
-        b, h, _, d = self._kbuf.shape
-        total = n_region + sum(p.shape[-2] for p in parts)
-        out = torch.empty(b, h, total, d, dtype=self.dtype, device=self.device)
-        if region is not None and n_region:
-            out[:, :, :n_region].copy_(region)
-        at = n_region
-        for p in parts:
-            out[:, :, at:at + p.shape[-2]].copy_(p)
-            at += p.shape[-2]
-        return out
-
     def _logical(self, t: int, chunk: tuple[torch.Tensor, torch.Tensor] | None = None):
         """(keys, values) of [region rotated to sit before the window, window by position,
-        chunk] for a query at position t."""
+        chunk] for a query at position t: the window rows and the region's values gathered by
+        one kernel launch (16-byte copies from the ring slots), the region's keys rotated
+        straight into the new tensor's first rows by the place kernel."""
         R = len(self._region)
         lo, hi = self._window_span(t)
-        kparts = self._ring_views(self._kbuf, lo, hi) + ([chunk[0]] if chunk is not None else [])
-        vparts = self._ring_views(self._vbuf, lo, hi) + ([chunk[1]] if chunk is not None else [])
-        keys = self._stack_rows(R, kparts, None)
-        if R:  # the region's keys, rotated straight into the new tensor's first rows
+        n = chunk[0].shape[-2] if chunk is not None else 0
+        b, h, _, d = self._kbuf.shape
+        rows = R + max(0, hi - lo) + n
+        keys = torch.empty(b, h, rows, d, dtype=self.dtype, device=self.device)
+        values = torch.empty(b, h, rows, d, dtype=self.dtype, device=self.device)
+        if R:
             _lib.v2_place(self._kbuf, self._vbuf, None, None, self._reg_k, self._reg_pos, R, keys[:, :, :R], None,
                           t, self.n_sink, self.window, self.inv_freq)
-        values = self._stack_rows(R, vparts, self._region.values[:, :, :R])
+        k_new, v_new = chunk if chunk is not None else (None, None)
+        if n and (not self._gatherable(k_new) or not self._gatherable(v_new)):
+            k_new, v_new = k_new.contiguous(), v_new.contiguous()
+        _lib.v2_gather(self._kbuf, self._vbuf, self.n_sink, self.window, R, lo, hi, k_new if n else None,
+                       v_new if n else None, keys, values)
         return keys, values
+
+    @staticmethod
+    def _gatherable(x: torch.Tensor) -> bool:
+        """Rows the gather kernel reads with 16-byte copies: unit last stride, 16-byte aligned."""
+        es = x.element_size()
+        return (x.stride(-1) == 1 and x.data_ptr() % 16 == 0
+                and all((st * es) % 16 == 0 for st in x.stride()[:-1]))
 
     # ------------------------------------------------------------------ pins
 

@@ -101,3 +101,78 @@ __global__ void __launch_bounds__(kThreads) sink_v2_place_kernel(V2PlaceArgs a) 
 }
 
 }  // namespace sinkb200
+
+namespace sinkb200 {
+
+// Rows a ring-buffer layer's multi-token step attends over, in the reference's order:
+// [region (R rows), window by position, chunk (n rows)].
+struct V2GatherArgs {
+  const char* kbuf;                  // ring + region slots, rows contiguous
+  const char* vbuf;
+  int64_t k_sb, k_sh, v_sb, v_sh;    // element strides
+  const char* knew;                  // [B, Hkv, n, D] the chunk, or null (n == 0)
+  const char* vnew;
+  int64_t kn_sb, kn_sh, kn_st, vn_sb, vn_sh, vn_st;
+  char* ok;                          // [B, Hkv, >= rows, D] outputs
+  char* ov;
+  int64_t ok_sb, ok_sh, ok_st, ov_sb, ov_sh, ov_st;
+  int64_t lo;                        // first window position (>= n_sink)
+  int n_sink, ring, R, nwin, n, rows, heads_kv, pairs;
+};
+
+// 16-byte words each thread of sink_v2_gather_kernel copies per round (loads before stores).
+constexpr int kGatherWordsPerThread = 4;
+
+// out rows r of every (batch, head): r < R: the region's value row (kv row ring + r; the
+// region's keys are rotated into out_k by the place kernel); R <= r < R + nwin: ring slot
+// (lo + r - R - n_sink) mod ring; then chunk row r - R - nwin.  One flat index over
+// (tensor, pair, row, 16-byte word), consecutive threads on consecutive words of a row.
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads) sink_v2_gather_kernel(const __grid_constant__ V2GatherArgs g) {
+  grid_dependency_wait();
+  allow_dependents();
+  constexpr int W = D * int(sizeof(T)) / 16;  // words per row
+  const long long per = (long long)g.pairs * g.rows * W;
+  const long long total = 2 * per;
+  constexpr int U = kGatherWordsPerThread;
+  const long long step = (long long)gridDim.x * kThreads * U;
+  for (long long tile = (long long)blockIdx.x * kThreads * U; tile < total; tile += step) {
+    uint4 w[U];
+    uint4* dst[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const long long i = tile + (long long)u * kThreads + threadIdx.x;
+      dst[u] = nullptr;
+      if (i >= total) continue;
+      const bool isv = i >= per;
+      const long long li = isv ? i - per : i;
+      const int c = int(li % W);
+      const long long rr = li / W;
+      const int r = int(rr % g.rows), p = int(rr / g.rows);
+      const int b = p / g.heads_kv, h = p - b * g.heads_kv;
+      const T* src;
+      if (r < g.R) {
+        if (!isv) continue;
+        src = reinterpret_cast<const T*>(g.vbuf) + b * g.v_sb + h * g.v_sh + (long long)(g.ring + r) * D;
+      } else if (r < g.R + g.nwin) {
+        long long slot = (g.lo + (r - g.R) - g.n_sink) % g.ring;
+        if (slot < 0) slot += g.ring;
+        src = isv ? reinterpret_cast<const T*>(g.vbuf) + b * g.v_sb + h * g.v_sh + slot * D
+                  : reinterpret_cast<const T*>(g.kbuf) + b * g.k_sb + h * g.k_sh + slot * D;
+      } else {
+        const int j = r - g.R - g.nwin;
+        src = isv ? reinterpret_cast<const T*>(g.vnew) + b * g.vn_sb + h * g.vn_sh + (long long)j * g.vn_st
+                  : reinterpret_cast<const T*>(g.knew) + b * g.kn_sb + h * g.kn_sh + (long long)j * g.kn_st;
+      }
+      T* d = isv ? reinterpret_cast<T*>(g.ov) + b * g.ov_sb + h * g.ov_sh + (long long)r * g.ov_st
+                 : reinterpret_cast<T*>(g.ok) + b * g.ok_sb + h * g.ok_sh + (long long)r * g.ok_st;
+      w[u] = reinterpret_cast<const uint4*>(src)[c];
+      dst[u] = reinterpret_cast<uint4*>(d) + c;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (dst[u] != nullptr) *dst[u] = w[u];
+  }
+}
+
+}  // namespace sinkb200

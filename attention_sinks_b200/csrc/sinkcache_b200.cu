@@ -1216,6 +1216,98 @@ int32_t sink_debug_fail_next_wait(int32_t chunk, int32_t polls) {
   return SINK_OK;
 }
 
+int32_t sink_v2_gather(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t window,
+                       int32_t region_len, int64_t lo, int64_t hi, const sink_rows_t* k_new,
+                       const sink_rows_t* v_new, const sink_rows_t* out_k, const sink_rows_t* out_v,
+                       void* stream) {
+  int32_t rc = check_kv(kv);
+  if (rc) return rc;
+  if (kv->k_dtype != kv->v_dtype) return SINK_EDTYPE;
+  const int es = elem_size(kv->k_dtype);
+  if (n_sink < 0 || window < 1 || region_len < 0) return SINK_EINVAL;
+  const int64_t ring = int64_t(window) + 1;
+  if (ring + region_len > kv->slots) return SINK_EINVAL;
+  const int64_t nwin = hi > lo ? hi - lo : 0;
+  if (nwin > 0 && (lo < n_sink || nwin > ring)) return SINK_EINVAL;
+  if ((k_new == nullptr) != (v_new == nullptr)) return SINK_EINVAL;
+  const int n = k_new ? k_new->n : 0;
+  if (k_new) {
+    if ((rc = check_rows(k_new, kv->v_dtype, kv->batch, kv->heads_kv, n))) return rc;
+    if ((rc = check_rows(v_new, kv->v_dtype, kv->batch, kv->heads_kv, n))) return rc;
+    if (!rows_aligned16(k_new, es) || !rows_aligned16(v_new, es) || ((k_new->stride_t * es) & 15) ||
+        ((v_new->stride_t * es) & 15))
+      return SINK_ELAYOUT;
+  }
+  const int64_t rows = region_len + nwin + n;
+  if (rows > INT_MAX) return SINK_EINVAL;
+  if (!out_k || !out_v) return SINK_EINVAL;
+  if ((rc = check_rows(out_k, kv->k_dtype, kv->batch, kv->heads_kv, out_k->n))) return rc;
+  if ((rc = check_rows(out_v, kv->v_dtype, kv->batch, kv->heads_kv, out_v->n))) return rc;
+  if (out_k->n < rows || out_v->n < rows) return SINK_EINVAL;
+  if (!rows_aligned16(out_k, es) || !rows_aligned16(out_v, es) || ((out_k->stride_t * es) & 15) ||
+      ((out_v->stride_t * es) & 15))
+    return SINK_ELAYOUT;
+  if (rows == 0) return SINK_OK;
+  V2GatherArgs g;
+  std::memset(&g, 0, sizeof(g));
+  g.kbuf = static_cast<const char*>(kv->k);
+  g.vbuf = static_cast<const char*>(kv->v);
+  g.k_sb = kv->k_stride_b;
+  g.k_sh = kv->k_stride_h;
+  g.v_sb = kv->v_stride_b;
+  g.v_sh = kv->v_stride_h;
+  if (k_new) {
+    g.knew = static_cast<const char*>(k_new->data);
+    g.vnew = static_cast<const char*>(v_new->data);
+    g.kn_sb = k_new->stride_b;
+    g.kn_sh = k_new->stride_h;
+    g.kn_st = k_new->stride_t;
+    g.vn_sb = v_new->stride_b;
+    g.vn_sh = v_new->stride_h;
+    g.vn_st = v_new->stride_t;
+  }
+  g.ok = static_cast<char*>(out_k->data);
+  g.ov = static_cast<char*>(out_v->data);
+  g.ok_sb = out_k->stride_b;
+  g.ok_sh = out_k->stride_h;
+  g.ok_st = out_k->stride_t;
+  g.ov_sb = out_v->stride_b;
+  g.ov_sh = out_v->stride_h;
+  g.ov_st = out_v->stride_t;
+  g.lo = lo;
+  g.n_sink = n_sink;
+  g.ring = int(ring);
+  g.R = region_len;
+  g.nwin = int(nwin);
+  g.n = n;
+  g.rows = int(rows);
+  g.heads_kv = kv->heads_kv;
+  g.pairs = kv->batch * kv->heads_kv;
+  int dev = 0;
+  const int sms = device_sms(&dev);
+  if (sms <= 0) return SINK_EDEVICE;
+  const long long words = 2LL * g.pairs * rows * (kv->head_dim * es / 16);
+  long long grid = (words + kThreads * kGatherWordsPerThread - 1) / (kThreads * kGatherWordsPerThread);
+  if (grid > 8LL * sms) grid = 8LL * sms;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto go = [&](auto kern) { return launch_dependent(kern, dim3(unsigned(grid)), 0, st, g); };
+  switch (kv->k_dtype) {
+    case SINK_DTYPE_BF16:
+      if (kv->head_dim == 64) return go(sink_v2_gather_kernel<__nv_bfloat16, 64>);
+      if (kv->head_dim == 128) return go(sink_v2_gather_kernel<__nv_bfloat16, 128>);
+      return go(sink_v2_gather_kernel<__nv_bfloat16, 256>);
+    case SINK_DTYPE_F16:
+      if (kv->head_dim == 64) return go(sink_v2_gather_kernel<__half, 64>);
+      if (kv->head_dim == 128) return go(sink_v2_gather_kernel<__half, 128>);
+      return go(sink_v2_gather_kernel<__half, 256>);
+    case SINK_DTYPE_F32:
+      if (kv->head_dim == 64) return go(sink_v2_gather_kernel<float, 64>);
+      if (kv->head_dim == 128) return go(sink_v2_gather_kernel<float, 128>);
+      return go(sink_v2_gather_kernel<float, 256>);
+    default: return SINK_EDTYPE;
+  }
+}
+
 int32_t sink_prepare_device(void) {
   int dev = 0;
   if (device_sms(&dev) <= 0) return SINK_EDEVICE;

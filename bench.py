@@ -510,9 +510,39 @@ def graph_floor(device: torch.device, flush: torch.Tensor, steps: int = 50) -> f
     return round(total / steps * 1e3, 2)
 
 
+def time_graph_layers(benches: list, reps: int = 30) -> float:
+    """Mean ms per layer-step of one CUDA graph holding one step of every bench in turn (each
+    its own state, like the layers of a model's decode step).  Their states together exceed
+    2x L2, so every step reads its state from HBM with no flush in between."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for b in benches:
+            b.step(0)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for b in benches:
+            b.step(0)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        graph.replay()
+    end.record()
+    end.synchronize()
+    return start.elapsed_time(end) / (reps * len(benches))
+
+
 def sweep(device: torch.device, flush: torch.Tensor, cls=None, alg=None) -> dict:
     """µs per layer-step and GB/s over the op-bench grid (slots x streams), 1 GPU, from
-    CUDA-graph replays (L2 flushed between replays when the state is smaller than 2x L2)."""
+    CUDA-graph replays.  `us_per_layer`: one step replayed alone, L2 overwritten before each
+    replay when the state is smaller than 2x L2 (so it carries a graph launch per step).
+    `us_per_layer_in_sequence`: for such states, the steps of as many independent layer
+    states as exceed 2.5x L2 together, captured in one graph and replayed back to back, the
+    way a model's layers run in one decode step; per layer-step."""
     cls, alg = cls or OpBench, alg or alg_bytes
     out = {}
     for slots in (256, 1024, 4096, 32768):
@@ -521,9 +551,17 @@ def sweep(device: torch.device, flush: torch.Tensor, cls=None, alg=None) -> dict
             small = b.state_bytes() < 2 * L2_BYTES
             steps = 50 if small else max(10, min(200, int(2e9 / (alg(slots) * batch))))
             ms = time_graph(b, steps, flush if small else None)
-            out[f"S{slots}_B{batch}"] = {"us_per_layer": round(ms * 1e3, 2),
-                                        "GB_s": round(alg(slots) * batch / (ms * 1e-3) / 1e9, 1),
-                                        "l2_flushed": small}
+            row = {"us_per_layer": round(ms * 1e3, 2), "GB_s": round(alg(slots) * batch / (ms * 1e-3) / 1e9, 1),
+                   "l2_flushed": small}
+            if small:
+                n = min(64, max(2, math.ceil(2.5 * L2_BYTES / b.state_bytes())))
+                layers = [b] + [cls(batch, slots, device, seed=slots + batch + 97 * i) for i in range(1, n)]
+                ms_seq = time_graph_layers(layers)
+                row["us_per_layer_in_sequence"] = round(ms_seq * 1e3, 2)
+                row["GB_s_in_sequence"] = round(alg(slots) * batch / (ms_seq * 1e-3) / 1e9, 1)
+                row["layers_in_sequence"] = n
+                del layers
+            out[f"S{slots}_B{batch}"] = row
             del b
             torch.cuda.empty_cache()
     return out

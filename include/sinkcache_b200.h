@@ -293,6 +293,24 @@ int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_ne
  */
 int32_t sink_debug_fail_next_wait(int32_t chunk, int32_t polls);
 
+/*
+ * The rows a ring-buffer layer's multi-token step attends over, in the reference's order
+ * [region (R rows), window by position, chunk (n rows)], gathered into out_k / out_v
+ * ([batch, heads_kv, >= R + (hi - lo) + n, head_dim], rows 16-byte aligned):
+ *   - rows [0, R): out_v gets the region's value rows (kv rows window + 1 ..); out_k is left
+ *     for sink_v2_place with region_out = those rows (the rotated region keys);
+ *   - rows [R, R + hi - lo): positions lo .. hi - 1 (>= n_sink, at most window + 1 of them)
+ *     from their ring slots (p - n_sink) mod (window + 1);
+ *   - the rest: the chunk's rows k_new / v_new (both or neither).
+ * kv: K and V in the model dtype.  16-byte copies, one launch for both tensors.
+ * Replaces the index_select / cat gathers of SinkLayerV2._general_step and kept()
+ * (src/sinkcache/cache_v2.py:189-193, 229-234).
+ */
+int32_t sink_v2_gather(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t window,
+                       int32_t region_len, int64_t lo, int64_t hi, const sink_rows_t* k_new,
+                       const sink_rows_t* v_new, const sink_rows_t* out_k, const sink_rows_t* out_v,
+                       void* stream);
+
 /* Size of the static device scratch behind sink_decode_attention_noalloc: 16 MiB. */
 #define SINK_NOALLOC_SCRATCH_BYTES (16u << 20)
 

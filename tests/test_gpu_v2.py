@@ -355,3 +355,32 @@ def test_streamed_nll_matches_reference(fused, golden, golden_arrays):
     torch.testing.assert_close(logits, torch.from_numpy(golden_arrays["v2_stream/last_logits"]), rtol=0, atol=2e-3)
     assert cache.tokens_evicted == want["tokens_evicted"] and cache.region_size == want["region_size"]
     assert cache.workspace.read_status() == 0
+
+
+@pytest.mark.parametrize("window,n_sink,R,t,n,d", [
+    (60, 4, 4, 200, 16, 128),      # window wraps around the ring's end
+    (60, 4, 12, 64, 0, 64),        # window exactly full, no chunk
+    (1020, 4, 4, 1500, 37, 128),
+    (30, 0, 0, 20, 5, 256),        # no sinks, window not full yet
+])
+def test_gather_matches_ring_order(window, n_sink, R, t, n, d):
+    """sink_v2_gather: [region values, window rows in position order, chunk] -- the rows the
+    reference gathers with index_select and cat (cache_v2.py:189-193) -- bit for bit."""
+    g = torch.Generator(device=DEV).manual_seed(window + t)
+    b, h = 2, 4
+    ring = window + 1
+    kbuf = torch.randn(b, h, ring + R + 3, d, device=DEV, generator=g).bfloat16()
+    vbuf = torch.randn(b, h, ring + R + 3, d, device=DEV, generator=g).bfloat16()
+    lo, hi = max(max(min(t, n_sink), t - window), n_sink), t
+    k = torch.randn(b, h, n, d, device=DEV, generator=g).bfloat16() if n else None
+    v = torch.randn(b, h, n, d, device=DEV, generator=g).bfloat16() if n else None
+    rows = R + max(0, hi - lo) + n
+    ok = torch.full((b, h, rows, d), 7.0, dtype=torch.bfloat16, device=DEV)
+    ov = torch.full((b, h, rows, d), 7.0, dtype=torch.bfloat16, device=DEV)
+    _lib.v2_gather(kbuf, vbuf, n_sink, window, R, lo, hi, k, v, ok, ov)
+    slots = torch.tensor([(p - n_sink) % ring for p in range(lo, hi)], dtype=torch.long, device=DEV)
+    want_k = torch.cat([kbuf.index_select(2, slots)] + ([k] if n else []), -2)
+    want_v = torch.cat([vbuf[:, :, ring:ring + R], vbuf.index_select(2, slots)] + ([v] if n else []), -2)
+    torch.testing.assert_close(ok[:, :, R:], want_k, rtol=0, atol=0)
+    torch.testing.assert_close(ov, want_v, rtol=0, atol=0)
+    assert bool((ok[:, :, :R] == 7.0).all())  # the region's keys are the place kernel's

@@ -33,6 +33,21 @@ def fake_place(kbuf, vbuf, k, v, reg_k, reg_pos, R, region_out, position, t, n_s
         position[0] += 1
 
 
+def fake_gather(kbuf, vbuf, n_sink, window, R, lo, hi, k, v, out_k, out_v):
+    ring = window + 1
+    if R:
+        out_v[:, :, :R] = vbuf[:, :, ring:ring + R]
+    nwin = max(0, hi - lo)
+    for i in range(nwin):
+        slot = (lo + i - n_sink) % ring
+        out_k[:, :, R + i] = kbuf[:, :, slot]
+        out_v[:, :, R + i] = vbuf[:, :, slot]
+    if k is not None:
+        n = k.shape[-2]
+        out_k[:, :, R + nwin:R + nwin + n] = k
+        out_v[:, :, R + nwin:R + nwin + n] = v
+
+
 def fake_decode_step(kbuf, vbuf, k, v, reg_k, reg_pos, R, position, n_sink, window, inv_freq, q, scale,
                      out, ws, mask=None):
     fake_place(kbuf, vbuf, k, v, reg_k, reg_pos, R, None, position, 0, n_sink, window, inv_freq)
@@ -57,6 +72,7 @@ def cpu_v2(monkeypatch):
     monkeypatch.setattr(_lib, "sm_count", lambda device: 148)
     monkeypatch.setattr(_lib, "v2_place", count("place", fake_place))
     monkeypatch.setattr(_lib, "v2_decode_step", count("fused", fake_decode_step))
+    monkeypatch.setattr(_lib, "v2_gather", fake_gather)
     monkeypatch.setattr(da, "_on_kernel_device", lambda q: True)
     return calls
 
