@@ -25,6 +25,7 @@ EXPORTED_SYMBOLS = (
     "sink_evict_rerotate", "sink_decode_attention", "sink_fused_decode_step", "sink_read_status",
     "sink_decode_attention_noalloc", "sink_v2_place", "sink_v2_decode_step", "sink_prepare_device",
     "sink_debug_fail_next_wait", "sink_plan_launch", "sink_evict_rerotate_keycopy", "sink_v2_gather",
+    "sink_debug_cluster_capacity", "sink_launch_count",
 )
 LAUNCH_SPLIT, LAUNCH_CLUSTER, LAUNCH_TENSOR = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 16 << 20
@@ -63,6 +64,7 @@ def _declare(lib):
     pi32 = ctypes.POINTER(ctypes.c_int32)
     sig = {
         "sink_abi_version": (i32, []),
+        "sink_launch_count": (ctypes.c_uint64, []),
         "sink_strerror": (ctypes.c_char_p, [i32]),
         "sink_workspace_bytes": (sz, [i32] * 12),
         "sink_plan": (i32, [i32] * 12 + [pi32] * 6),
@@ -76,6 +78,7 @@ def _declare(lib):
         "sink_read_status": (i32, [vp, vp, pi32]),
         "sink_prepare_device": (i32, []),
         "sink_debug_fail_next_wait": (i32, [i32, i32]),
+        "sink_debug_cluster_capacity": (i32, [i32]),
         "sink_decode_attention_noalloc": (i32, [prows, pkv, i32, ctypes.c_float, vp, i64, vp, i64, i64, vp]),
         "sink_v2_place": (i32, [pkv, prows, prows, prows, vp, i32, prows, vp, i64, i32, i32, vp, i32, vp]),
         "sink_v2_gather": (i32, [pkv, i32, i32, i32, i64, i64, prows, prows, prows, prows, vp]),
@@ -253,6 +256,18 @@ def fail_next_wait(chunk: int, polls: int) -> None:
     leaves chunk `chunk` of every split unissued, with every wait bounded by `polls` polls,
     so that wait runs out and the launch reports SINK_STATUS_WAIT_TIMEOUT."""
     _check(lib().sink_debug_fail_next_wait(int(chunk), int(polls)), "sink_debug_fail_next_wait")
+
+
+def launch_count() -> int:
+    """Kernel launches the library has issued in this process (sink_launch_count)."""
+    return int(lib().sink_launch_count())
+
+
+def force_cluster_capacity(clusters: int) -> None:
+    """Cluster-fallback test hook (sink_debug_cluster_capacity): clusters >= 0 is taken as the
+    device's capacity for every clustered stream launch (0: clustered plans run as split
+    launches); -1 asks the device again."""
+    _check(lib().sink_debug_cluster_capacity(int(clusters)), "sink_debug_cluster_capacity")
 
 
 def append(kbuf: torch.Tensor, vbuf: torch.Tensor, k: torch.Tensor, v: torch.Tensor, row: int) -> None:

@@ -4,8 +4,8 @@
 //
 // Persistent: one CTA (192 threads) per SM (the pipeline takes 192 KB of shared memory)
 // walks the work items (split, batch * kv-head) i = blockIdx.x, blockIdx.x + gridDim.x, ...
-// as one continuous stream of 128-row key chunks, so the copy pipeline stays full across
-// item boundaries.  Per chunk:
+// (tc_item) as one continuous stream of 128-row key chunks, so the copy pipeline stays full
+// across item boundaries.  Per chunk:
 //   - TMA (cp.async.bulk.tensor, 4-D maps over [B, Hkv, slots, 128], 128-byte swizzle)
 //     loads the chunk's K and V as two 64-column boxes each into one of 3 stages;
 //   - one thread issues S^T = K . Q^T as 8 tcgen05.mma (M = 128 keys, N = 16 query rows of
@@ -33,6 +33,7 @@
 #include <type_traits>
 
 #include "sink_chunk.cuh"
+#include "sink_v2.cuh"
 
 namespace sinkb200 {
 
@@ -69,6 +70,11 @@ struct TcArgs {
   // 1: one item per CTA and the ns CTAs of each pair launched as one cluster; the pair's
   // split partials are merged at the end of the kernel (no sink_combine_kernel launch).
   int cluster;
+  // 1: the ring-buffer step's place work runs first, each CTA on the rows of its own items
+  // (no row belongs to two items), and the device position advances as in
+  // sink_v2_place_kernel: the v2 decode step in one launch.
+  int place;
+  V2PlaceArgs pa;
 };
 
 // Largest cluster (a pair's splits) for the in-cluster merge; sizes above 8 are used only
@@ -192,15 +198,24 @@ __device__ __forceinline__ uint32_t tc_operand_offset(int r, int c) {
 
 // ------------------------------------------------------------------ kernel
 
-// Item `it` = (split j, pair p): its (batch, head), rows [a, e) and chunk count.
+// Item `it` = (split j, pair p): its (batch, head), rows [a, e) and chunk count.  Pair-major
+// (it = p * ns + j), except with the place work fused in: split-major (it = j * pairs + p),
+// so that the pairs' items over the same rows -- the last split's region rows, the split
+// holding this step's ring slot -- are consecutive and land on different CTAs.  A clustered
+// launch (its clusters are the pairs) is always pair-major.
 struct TcItem {
   int p, j, b, h, a, e, n;
 };
 
 __device__ __forceinline__ TcItem tc_item(const TcArgs& A, int it) {
   TcItem w;
-  w.p = it / A.ns;
-  w.j = it - w.p * A.ns;
+  if (A.cluster || !A.place) {
+    w.p = it / A.ns;
+    w.j = it - w.p * A.ns;
+  } else {
+    w.j = it / A.pairs;
+    w.p = it - w.j * A.pairs;
+  }
   w.b = w.p / A.heads_kv;
   w.h = w.p - w.b * A.heads_kv;
   split_rows(0, A.row_end, A.rows_per_split, w.j, w.a, w.e);
@@ -272,6 +287,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
   float* red2 = red + 32;                                               // [4 warps][8]: item sums
   int* flag = reinterpret_cast<int*>(red2 + 32);                        // CTA failure flag
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red2 + 40);
+  long long* t_s = reinterpret_cast<long long*>(red2 + 42);             // place: the position t
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = A.group;
@@ -326,6 +342,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
   auto tmem_o = [&](int item_ord) { return tmem + 2 * kTcN + (item_ord & 1) * kTcN; };
 
   grid_dependency_wait();  // the producers of q and of the cache rows are complete
+
+  if (A.place) {
+    if (tid == 0) *t_s = A.pa.position ? A.pa.position[0] : A.pa.t_host;
+    __syncthreads();
+    const long long t = *t_s;
+    const long long ws = v2_window_start(A.pa, t);
+    for (int ord = 0; ord < my_items; ++ord) {
+      const TcItem w = item_of(ord);
+      v2_place_pair<T, kTcD>(A.pa, w.b, w.h, t, ws, w.a, w.e, tid, kTcThreads);
+    }
+    fence_proxy_async_global();  // the TMA loads below read the placed rows
+    __syncthreads();
+    if (tid == 0 && A.pa.position) v2_position_arrive(A.pa, t);
+  }
 
   bool failed = false;
   if (warp == kTcLoadWarp) {

@@ -195,6 +195,12 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Orders this thread's generic-proxy global stores before async-proxy (TMA) accesses that a
+// later barrier makes depend on them.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Programmatic dependent launch: a kernel launched with programmatic stream serialization
 // may start before its predecessor ends; grid_dependency_wait() blocks until the
 // predecessor grid has completed and its memory is visible.  allow_dependents() lets the

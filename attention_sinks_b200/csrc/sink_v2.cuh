@@ -28,32 +28,32 @@ struct V2PlaceArgs {
   int n_sink, window, ring, R, rot_half, heads_kv, pairs;
 };
 
-// One CTA per (batch, kv-head) pair (grid-strided).  t is the absolute position of the new
-// token; ws = max(min(t, n_sink), t - window) the first window position; region row j is
-// rotated by (ws - R + j) - reg_pos[j].  The angle is formed in fp64 (positions grow without
-// bound), cos/sin rounded once to fp32, and each output element is
-// fp32(fp32(x * cos) + fp32(rotate_half(x) * sin)) rounded once to the storage type: the
-// reference's three separately rounded tensor ops.  With `position`, the last CTA to finish
-// stores t + 1 (every CTA has read t before it counts itself in).
-template <typename T, int D>
-__global__ void __launch_bounds__(kThreads) sink_v2_place_kernel(V2PlaceArgs a) {
-  grid_dependency_wait();
-  allow_dependents();
-  __shared__ long long t_s;
-  if (threadIdx.x == 0) t_s = a.position ? a.position[0] : a.t_host;
-  __syncthreads();
-  const long long t = t_s;
+// First window position when the next token is t.
+__device__ __forceinline__ long long v2_window_start(const V2PlaceArgs& a, long long t) {
   long long ws = t < a.n_sink ? t : a.n_sink;
   if (t - a.window > ws) ws = t - a.window;
+  return ws;
+}
+
+// The place work of one (batch, kv-head) pair, limited to its rows [row_lo, row_hi) of the
+// kv buffers (ring slots, then the region rows from `ring`): the new token into ring slot
+// (t - n_sink) mod ring when that slot is in range, and the region rows j (kv row ring + j,
+// or region_out row j) in range rotated from their originals.  Region row j is rotated by
+// (ws - R + j) - reg_pos[j]; the angle is formed in fp64 (positions grow without bound),
+// cos/sin rounded once to fp32, and each output element is fp32(fp32(x * cos) +
+// fp32(rotate_half(x) * sin)) rounded once to the storage type: the reference's three
+// separately rounded tensor ops.  Threads `tid` of `nthreads` share the work.
+template <typename T, int D>
+__device__ __forceinline__ void v2_place_pair(const V2PlaceArgs& a, int b, int h, long long t, long long ws,
+                                              int row_lo, int row_hi, int tid, int nthreads) {
   using E = Elem<T>;
   constexpr int kVec = 16 / sizeof(T);   // elements per 16-byte vector
   constexpr int kRowVecs = D / kVec;
-  for (int p = blockIdx.x; p < a.pairs; p += gridDim.x) {
-    const int b = p / a.heads_kv, h = p - b * a.heads_kv;
-    if (a.knew) {
-      long long slot = (t - a.n_sink) % a.ring;
-      if (slot < 0) slot += a.ring;
-      for (int i = threadIdx.x; i < 2 * kRowVecs; i += kThreads) {
+  if (a.knew) {
+    long long slot = (t - a.n_sink) % a.ring;
+    if (slot < 0) slot += a.ring;
+    if (slot >= row_lo && slot < row_hi) {
+      for (int i = tid; i < 2 * kRowVecs; i += nthreads) {
         const bool is_v = i >= kRowVecs;
         const int c = is_v ? i - kRowVecs : i;
         const T* src = reinterpret_cast<const T*>(is_v ? a.vnew : a.knew) +
@@ -63,40 +63,63 @@ __global__ void __launch_bounds__(kThreads) sink_v2_place_kernel(V2PlaceArgs a) 
         reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(src)[c];
       }
     }
-    const T* rk = reinterpret_cast<const T*>(a.reg_k) + b * a.rk_sb + h * a.rk_sh;
-    T* ro = reinterpret_cast<T*>(a.rout) + b * a.ro_sb + h * a.ro_sh;
-    const int rh = a.rot_half, pass = D - 2 * rh;
-    const int per_row = rh + pass;
-    for (int i = threadIdx.x; i < a.R * per_row; i += kThreads) {
-      const int j = i / per_row, c = i - j * per_row;
-      const T* x = rk + j * a.rk_st;
-      T* y = ro + j * a.ro_st;
-      if (c < rh) {
-        const long long delta = ws - a.R + j - a.reg_pos[j];
-        const double ang = __dmul_rn(static_cast<double>(delta), a.inv_freq[c]);
-        const float cs = __double2float_rn(cos(ang));
-        const float sn = __double2float_rn(sin(ang));
-        const float x1 = E::to_f(x[c]), x2 = E::to_f(x[c + rh]);
-        y[c] = E::from_f(__fadd_rn(__fmul_rn(x1, cs), __fmul_rn(-x2, sn)));
-        y[c + rh] = E::from_f(__fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn)));
-      } else {
-        const int d = 2 * rh + (c - rh);
-        y[d] = x[d];
-      }
+  }
+  const int j0 = row_lo - a.ring > 0 ? row_lo - a.ring : 0;
+  const int j1 = row_hi - a.ring < a.R ? row_hi - a.ring : a.R;
+  if (j0 >= j1) return;
+  const T* rk = reinterpret_cast<const T*>(a.reg_k) + b * a.rk_sb + h * a.rk_sh;
+  T* ro = reinterpret_cast<T*>(a.rout) + b * a.ro_sb + h * a.ro_sh;
+  const int rh = a.rot_half, pass = D - 2 * rh;
+  const int per_row = rh + pass;
+  for (int i = tid; i < (j1 - j0) * per_row; i += nthreads) {
+    const int j = j0 + i / per_row, c = i % per_row;
+    const T* x = rk + j * a.rk_st;
+    T* y = ro + j * a.ro_st;
+    if (c < rh) {
+      const long long delta = ws - a.R + j - a.reg_pos[j];
+      const double ang = __dmul_rn(static_cast<double>(delta), a.inv_freq[c]);
+      const float cs = __double2float_rn(cos(ang));
+      const float sn = __double2float_rn(sin(ang));
+      const float x1 = E::to_f(x[c]), x2 = E::to_f(x[c + rh]);
+      y[c] = E::from_f(__fadd_rn(__fmul_rn(x1, cs), __fmul_rn(-x2, sn)));
+      y[c + rh] = E::from_f(__fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn)));
+    } else {
+      const int d = 2 * rh + (c - rh);
+      y[d] = x[d];
     }
+  }
+}
+
+// Counts this CTA in on the device position after it has read t: the last CTA of the grid to
+// arrive stores t + 1 and clears the counter (no CTA waits for another).
+__device__ __forceinline__ void v2_position_arrive(const V2PlaceArgs& a, long long t) {
+  __threadfence();
+  const unsigned long long prev = atomicAdd(reinterpret_cast<unsigned long long*>(a.position + 1), 1ull);
+  if (prev == gridDim.x - 1) {
+    a.position[0] = t + 1;
+    a.position[1] = 0;
+    __threadfence();
+  }
+}
+
+// One CTA per (batch, kv-head) pair (grid-strided): the whole place step of each pair (the new
+// token, every region row).  With `position`, the last CTA to finish stores t + 1.
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads) sink_v2_place_kernel(V2PlaceArgs a) {
+  grid_dependency_wait();
+  allow_dependents();
+  __shared__ long long t_s;
+  if (threadIdx.x == 0) t_s = a.position ? a.position[0] : a.t_host;
+  __syncthreads();
+  const long long t = t_s;
+  const long long ws = v2_window_start(a, t);
+  for (int p = blockIdx.x; p < a.pairs; p += gridDim.x) {
+    const int b = p / a.heads_kv, h = p - b * a.heads_kv;
+    v2_place_pair<T, D>(a, b, h, t, ws, 0, a.ring + a.R, threadIdx.x, kThreads);
   }
   if (a.position) {
     __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence();
-      const unsigned long long prev =
-          atomicAdd(reinterpret_cast<unsigned long long*>(a.position + 1), 1ull);
-      if (prev == gridDim.x - 1) {
-        a.position[0] = t + 1;
-        a.position[1] = 0;
-        __threadfence();
-      }
-    }
+    if (threadIdx.x == 0) v2_position_arrive(a, t);
   }
 }
 

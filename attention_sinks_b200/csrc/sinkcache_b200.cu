@@ -3,6 +3,9 @@
 #include <atomic>
 #include <climits>
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include <cudaTypedefs.h>
 
@@ -228,8 +231,10 @@ int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
     if (drop > 0 && (op == SINK_OP_EVICT || op == SINK_OP_FUSED_STEP)) limit_halo(nrows, drop, pl);
     choose_cluster(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, drop, pl);
   }
+  // Partials and halo rows are reserved for clustered plans too: a device that cannot place
+  // the cluster runs the same plan as a split launch (settle_cluster).
   size_t off = 256;  // status word
-  if (attend && pl.ns > 1 && !pl.cluster) {
+  if (attend && pl.ns > 1) {
     const size_t parts = size_t(pairs) * pl.ns * G;
     pl.off_o = off;
     off += align256(parts * D * 4);
@@ -239,7 +244,7 @@ int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
     off += align256(parts * 4);
   }
   const bool evicts = op == SINK_OP_EVICT || op == SINK_OP_FUSED_STEP;
-  if (evicts && drop > 0 && pl.ns > 1 && !pl.cluster) {
+  if (evicts && drop > 0 && pl.ns > 1) {
     pl.halo_rows = drop < pl.rows_per_split ? drop : pl.rows_per_split;
     const size_t hrows = size_t(pairs) * pl.ns * pl.halo_rows;
     pl.off_hk = off;
@@ -292,6 +297,14 @@ int32_t check_rows(const sink_rows_t* r, int32_t dtype, int32_t batch, int32_t h
   return SINK_OK;
 }
 
+// Kernel launches this library has issued in the process (sink_launch_count).
+std::atomic<uint64_t> g_launches{0};
+
+cudaError_t counted(cudaError_t err) {
+  if (err == cudaSuccess) g_launches.fetch_add(1, std::memory_order_relaxed);
+  return err;
+}
+
 // Launch with programmatic stream serialization: the kernel may begin launching while its
 // predecessor in the stream finishes (every kernel here waits on the grid dependency before
 // touching memory), which hides the launch gap between the halo, stream and combine kernels.
@@ -319,7 +332,7 @@ int32_t launch_dependent_c(void (*kern)(Params...), dim3 grid, int threads, int 
   cfg.numAttrs = n;
   const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, args...);
   if (err != cudaSuccess) return err;
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 template <typename... Params, typename... Args>
@@ -345,8 +358,56 @@ constexpr int cluster_warps() {
 // consumed by the next stream-kernel launch of the process; -1 when disarmed.
 std::atomic<int64_t> g_fail_next_wait{-1};
 
+// Cluster placement override (sink_debug_cluster_capacity): -1 asks the device; n >= 0 is
+// taken as every clustered stream launch's capacity.
+std::atomic<int> g_cluster_capacity_override{-1};
+
+// How many clusters of `ns` CTAs of `kern` (threads, smem) the device holds at once, from
+// cudaOccupancyMaxActiveClusters, remembered per (device, kernel, ns).  A miss while the
+// stream is being captured is not queried (the launch is taken to fit, as it did eagerly).
+template <typename K>
+int cluster_capacity(K kern, int threads, int smem, int ns, int dev, cudaStream_t st) {
+  const int forced = g_cluster_capacity_override.load(std::memory_order_relaxed);
+  if (forced >= 0) return forced;
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int>, int> known;
+  const auto key = std::make_tuple(dev, reinterpret_cast<const void*>(kern), ns);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto it = known.find(key);
+    if (it != known.end()) return it->second;
+  }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    (void)cudaGetLastError();
+    return INT_MAX;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(ns));
+  cfg.blockDim = dim3(unsigned(threads));
+  cfg.dynamicSmemBytes = size_t(smem);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(ns);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
+    clusters = 0;
+    (void)cudaGetLastError();
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  known[key] = clusters;
+  return clusters;
+}
+
+// With `capacity`, nothing is launched: *capacity = how many of the plan's clusters the
+// device holds at once (the plan must be clustered).
 template <typename KT, typename VT, int D, int GMAX, bool ATTEND>
-int32_t launch_stream(const StreamArgs& A0, const Plan& pl, int pairs, cudaStream_t st, int dev) {
+int32_t launch_stream(const StreamArgs& A0, const Plan& pl, int pairs, cudaStream_t st, int dev,
+                      int* capacity = nullptr) {
   StreamArgs A = A0;
   const int64_t inject = g_fail_next_wait.exchange(-1, std::memory_order_acq_rel);
   if (inject >= 0) {
@@ -365,45 +426,69 @@ int32_t launch_stream(const StreamArgs& A0, const Plan& pl, int pairs, cudaStrea
   if (pl.cluster && (pl.ns > kClusterMax || A.cluster != 1)) return SINK_EINVAL;
   // only clustered launches stage halo rows and receive the cluster's partials in shared memory
   const int smem = pl.cluster ? Gm::SMEM : Gm::SMEM - Gm::HALO - Gm::MERGE;
+  if (capacity) {
+    if (!pl.cluster) return SINK_EINVAL;
+    *capacity = cluster_capacity(kern, threads, smem, pl.ns, dev, st);
+    return SINK_OK;
+  }
   return launch_dependent_c(kern, dim3(pl.ns, pairs), threads, smem, pl.cluster ? pl.ns : 1, st, A);
 }
 
 template <bool ATTEND, typename KT, typename VT, int D>
-int32_t by_group(int G, const StreamArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev) {
+int32_t by_group(int G, const StreamArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev, int* cap) {
   if constexpr (!ATTEND) {
     (void)G;
-    return launch_stream<KT, VT, D, 1, false>(A, pl, pairs, st, dev);
+    return launch_stream<KT, VT, D, 1, false>(A, pl, pairs, st, dev, cap);
   } else {
-    if (G <= 1) return launch_stream<KT, VT, D, 1, true>(A, pl, pairs, st, dev);
-    if (G <= 2) return launch_stream<KT, VT, D, 2, true>(A, pl, pairs, st, dev);
-    if (G <= 4) return launch_stream<KT, VT, D, 4, true>(A, pl, pairs, st, dev);
-    return launch_stream<KT, VT, D, 8, true>(A, pl, pairs, st, dev);
+    if (G <= 1) return launch_stream<KT, VT, D, 1, true>(A, pl, pairs, st, dev, cap);
+    if (G <= 2) return launch_stream<KT, VT, D, 2, true>(A, pl, pairs, st, dev, cap);
+    if (G <= 4) return launch_stream<KT, VT, D, 4, true>(A, pl, pairs, st, dev, cap);
+    return launch_stream<KT, VT, D, 8, true>(A, pl, pairs, st, dev, cap);
   }
 }
 
 template <bool ATTEND, typename KT, typename VT>
-int32_t by_dim(int D, int G, const StreamArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev) {
+int32_t by_dim(int D, int G, const StreamArgs& A, const Plan& pl, int pairs, cudaStream_t st, int dev, int* cap) {
   switch (D) {
-    case 64: return by_group<ATTEND, KT, VT, 64>(G, A, pl, pairs, st, dev);
-    case 128: return by_group<ATTEND, KT, VT, 128>(G, A, pl, pairs, st, dev);
-    case 256: return by_group<ATTEND, KT, VT, 256>(G, A, pl, pairs, st, dev);
+    case 64: return by_group<ATTEND, KT, VT, 64>(G, A, pl, pairs, st, dev, cap);
+    case 128: return by_group<ATTEND, KT, VT, 128>(G, A, pl, pairs, st, dev, cap);
+    case 256: return by_group<ATTEND, KT, VT, 256>(G, A, pl, pairs, st, dev, cap);
     default: return SINK_EHEADDIM;
   }
 }
 
 template <bool ATTEND>
 int32_t dispatch_stream(int kdt, int vdt, int D, int G, const StreamArgs& A, const Plan& pl,
-                        int pairs, cudaStream_t st, int dev) {
+                        int pairs, cudaStream_t st, int dev, int* cap = nullptr) {
   if (vdt == SINK_DTYPE_BF16) {
-    if (kdt == SINK_DTYPE_F32) return by_dim<ATTEND, float, __nv_bfloat16>(D, G, A, pl, pairs, st, dev);
-    if (kdt == SINK_DTYPE_BF16) return by_dim<ATTEND, __nv_bfloat16, __nv_bfloat16>(D, G, A, pl, pairs, st, dev);
+    if (kdt == SINK_DTYPE_F32) return by_dim<ATTEND, float, __nv_bfloat16>(D, G, A, pl, pairs, st, dev, cap);
+    if (kdt == SINK_DTYPE_BF16) return by_dim<ATTEND, __nv_bfloat16, __nv_bfloat16>(D, G, A, pl, pairs, st, dev, cap);
   } else if (vdt == SINK_DTYPE_F16) {
-    if (kdt == SINK_DTYPE_F32) return by_dim<ATTEND, float, __half>(D, G, A, pl, pairs, st, dev);
-    if (kdt == SINK_DTYPE_F16) return by_dim<ATTEND, __half, __half>(D, G, A, pl, pairs, st, dev);
+    if (kdt == SINK_DTYPE_F32) return by_dim<ATTEND, float, __half>(D, G, A, pl, pairs, st, dev, cap);
+    if (kdt == SINK_DTYPE_F16) return by_dim<ATTEND, __half, __half>(D, G, A, pl, pairs, st, dev, cap);
   } else if (vdt == SINK_DTYPE_F32) {
-    if (kdt == SINK_DTYPE_F32) return by_dim<ATTEND, float, float>(D, G, A, pl, pairs, st, dev);
+    if (kdt == SINK_DTYPE_F32) return by_dim<ATTEND, float, float>(D, G, A, pl, pairs, st, dev, cap);
   }
   return SINK_EDTYPE;
+}
+
+// A clustered plan whose cluster the device cannot place at all (a part or partition with
+// fewer SMs per GPC than the cluster needs) runs as the split launch of the same plan:
+// halo pre-pass, unclustered stream kernel, combine.  The workspace already holds the split
+// launch's partials and halo rows.
+template <bool ATTEND>
+int32_t settle_cluster(const sink_kv_buffers_t* kv, int G, StreamArgs& A, Plan& pl, int pairs,
+                       cudaStream_t st, int dev) {
+  if (!pl.cluster) return SINK_OK;
+  int capacity = 0;
+  const int32_t rc = dispatch_stream<ATTEND>(kv->k_dtype, kv->v_dtype, kv->head_dim, G, A, pl, pairs, st, dev,
+                                             &capacity);
+  if (rc) return rc;
+  if (capacity < 1) {
+    pl.cluster = false;
+    A.cluster = 0;
+  }
+  return SINK_OK;
 }
 
 template <typename VT>
@@ -447,7 +532,7 @@ int32_t launch_halo(const sink_kv_buffers_t* kv, const StreamArgs& A, const Plan
   long cx = (words + kThreads * kHaloWordsPerThread - 1) / (kThreads * kHaloWordsPerThread);
   if (cx > 65535) cx = 65535;
   sink_halo_kernel<<<dim3(unsigned(cx), pairs), kThreads, 0, st>>>(A, H);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 void fill_common(StreamArgs& A, const sink_kv_buffers_t* kv, const Plan& pl, char* ws) {
@@ -589,12 +674,19 @@ int32_t launch_tc_t(int G, const TcArgs& A, const Plan& pl, int pairs, cudaStrea
   return launch_tc_g<T, 8>(A, pl, pairs, st, dev, merged);
 }
 
+// With `place`, the kernel runs the ring-buffer step's place work first (the v2 decode step
+// in one launch).
 int32_t launch_attention_tc(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows,
                             float scale, const uint8_t* mask, int64_t mask_stride_b, void* out,
                             int64_t out_stride_b, int64_t out_stride_h, void* workspace,
-                            const Plan& pl, int dev, cudaStream_t st) {
+                            const Plan& pl, int dev, cudaStream_t st,
+                            const V2PlaceArgs* place = nullptr) {
   TcArgs A;
   std::memset(&A, 0, sizeof(A));
+  if (place) {
+    A.place = 1;
+    A.pa = *place;
+  }
   int32_t rc = encode_cache_map(&A.kmap, kv->k, kv->k_dtype, kv, kv->k_stride_b, kv->k_stride_h);
   if (rc) return rc;
   if ((rc = encode_cache_map(&A.vmap, kv->v, kv->v_dtype, kv, kv->v_stride_b, kv->v_stride_h))) return rc;
@@ -646,10 +738,11 @@ int32_t launch_attention_tc(const sink_rows_t* q, const sink_kv_buffers_t* kv, i
 int32_t launch_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows,
                          float scale, const uint8_t* mask, int64_t mask_stride_b, void* out,
                          int64_t out_stride_b, int64_t out_stride_h, void* workspace,
-                         const Plan& pl, int dev, cudaStream_t st) {
+                         const Plan& pl, int dev, cudaStream_t st, const V2PlaceArgs* place = nullptr) {
   if (pl.tc)
     return launch_attention_tc(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
-                               out_stride_h, workspace, pl, dev, st);
+                               out_stride_h, workspace, pl, dev, st, place);
+  if (place) return SINK_EINVAL;
   int32_t rc;
   StreamArgs A;
   fill_common(A, kv, pl, static_cast<char*>(workspace));
@@ -668,9 +761,11 @@ int32_t launch_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int3
   A.mask = mask;
   A.mask_sb = mask_stride_b;
   const int pairs = kv->batch * kv->heads_kv;
-  if ((rc = dispatch_stream<true>(kv->k_dtype, kv->v_dtype, kv->head_dim, A.group, A, pl, pairs, st, dev)))
+  Plan pe = pl;
+  if ((rc = settle_cluster<true>(kv, A.group, A, pe, pairs, st, dev))) return rc;
+  if ((rc = dispatch_stream<true>(kv->k_dtype, kv->v_dtype, kv->head_dim, A.group, A, pe, pairs, st, dev)))
     return rc;
-  if (pl.ns > 1 && !pl.cluster) return launch_combine(kv->v_dtype, kv->head_dim, A, pairs, st);
+  if (pe.ns > 1 && !pe.cluster) return launch_combine(kv->v_dtype, kv->head_dim, A, pairs, st);
   return SINK_OK;
 }
 
@@ -686,7 +781,7 @@ int32_t launch_append_t(const sink_kv_buffers_t* kv, const sink_rows_t* kn, cons
       kv->v_stride_b, kv->v_stride_h, static_cast<const VT*>(kn->data),
       static_cast<const VT*>(vn->data), kn->stride_b, kn->stride_h, kn->stride_t, vn->stride_b,
       vn->stride_h, vn->stride_t, kv->heads_kv, kn->n, kv->head_dim, row, total);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 
@@ -929,6 +1024,8 @@ extern "C" {
 
 int32_t sink_abi_version(void) { return SINK_ABI_VERSION; }
 
+uint64_t sink_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
 const char* sink_strerror(int32_t code) {
   switch (code) {
     case SINK_OK: return "ok";
@@ -1064,6 +1161,7 @@ int32_t evict_launch(const sink_kv_buffers_t* kv, int32_t n_sink, int32_t window
   }
   const int pairs = kv->batch * kv->heads_kv;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = settle_cluster<false>(kv, 1, A, pl, pairs, st, dev))) return rc;
   if ((rc = launch_halo(kv, A, pl, pairs, st))) return rc;
   return dispatch_stream<false>(kv->k_dtype, kv->v_dtype, kv->head_dim, 1, A, pl, pairs, st, dev);
 }
@@ -1162,6 +1260,7 @@ int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k
   A.mask_sb = mask_stride_b;
   const int pairs = kv->batch * kv->heads_kv;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = settle_cluster<true>(kv, A.group, A, pl, pairs, st, dev))) return rc;
   if ((rc = launch_halo(kv, A, pl, pairs, st))) return rc;
   if ((rc = dispatch_stream<true>(kv->k_dtype, kv->v_dtype, kv->head_dim, A.group, A, pl, pairs, st, dev)))
     return rc;
@@ -1186,6 +1285,8 @@ int32_t sink_v2_place(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
   return launch_v2_place(kv, a, sms, static_cast<cudaStream_t>(stream));
 }
 
+constexpr long kFusedPlaceChunksPerCta = 32;
+
 int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
                             const sink_rows_t* v_new, const sink_rows_t* region_keys,
                             const int64_t* region_pos, int32_t region_len, int64_t* position,
@@ -1203,11 +1304,29 @@ int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_ne
   Plan pl;
   int dev = 0;
   if ((rc = plan_attention(q, kv, rows, out, workspace, workspace_bytes, pl, &dev))) return rc;
-  const int sms = device_sms(&dev);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int sms = device_sms(&dev);
+  if (sms <= 0) return SINK_EDEVICE;
+  // One launch where each tensor-core CTA places the rows of its own items first: with no
+  // more pairs than CTAs, no CTA owns more than one region item and one ring-slot item (the
+  // items of one split are consecutive).  Only for short steps: where the other CTAs keep
+  // HBM saturated for long, the owners' place loads queue behind their streams and those
+  // CTAs finish last, while the place kernel runs on an idle memory system (32,768 slots x
+  // 8 streams: 180 us fused, 176 us with the place kernel; 4,096 x 8: 37.0 against 37.9).
+  // More pairs, or more than kFusedPlaceChunksPerCta chunks per CTA, keep the place kernel.
+  const long chunks = long(a.pairs) * ((rows + kTcRows - 1) / kTcRows);
+  if (pl.tc && a.pairs <= sms && chunks <= kFusedPlaceChunksPerCta * long(sms))
+    return launch_attention(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
+                            out_stride_h, workspace, pl, dev, st, &a);
   if ((rc = launch_v2_place(kv, a, sms, st))) return rc;
   return launch_attention(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
                           out_stride_h, workspace, pl, dev, st);
+}
+
+int32_t sink_debug_cluster_capacity(int32_t clusters) {
+  if (clusters < -1) return SINK_EINVAL;
+  g_cluster_capacity_override.store(clusters, std::memory_order_relaxed);
+  return SINK_OK;
 }
 
 int32_t sink_debug_fail_next_wait(int32_t chunk, int32_t polls) {

@@ -26,12 +26,14 @@ from __future__ import annotations
 
 import torch
 
+from . import _lib
+
 
 class _CapturedStep:
     """One captured one-token step: the graph, the static tensors it reads (token ids,
     position ids) and writes (logits), and the cache layout it was captured against."""
 
-    __slots__ = ("graph", "ids", "positions", "logits", "signature")
+    __slots__ = ("graph", "ids", "positions", "logits", "signature", "cache_kernels")
 
     def __init__(self, signature, ids: torch.Tensor, positions: torch.Tensor | None):
         self.graph = torch.cuda.CUDAGraph()
@@ -39,6 +41,7 @@ class _CapturedStep:
         self.ids = ids
         self.positions = positions
         self.logits = None
+        self.cache_kernels = 0  # the sink-cache library's kernels in the graph
 
     def run(self, ids: torch.Tensor, position: int) -> torch.Tensor:
         self.ids.copy_(ids)
@@ -70,6 +73,12 @@ class StreamRunner:
     def graph(self) -> torch.cuda.CUDAGraph | None:
         """The graph of the current layout, if one has been captured."""
         return None if self._captured is None else self._captured.graph
+
+    @property
+    def cache_kernels_per_replay(self) -> int | None:
+        """How many of the sink-cache library's kernels one replay launches (counted by the
+        library while the step was captured), if a step has been captured."""
+        return None if self._captured is None else self._captured.cache_kernels
 
     @torch.no_grad()
     def step(self, ids: torch.Tensor) -> torch.Tensor:
@@ -108,8 +117,10 @@ class StreamRunner:
             kwargs["position_ids"] = positions
         captured = _CapturedStep(signature, ids.clone(), positions)
         torch.cuda.synchronize(ids.device)
+        launched = _lib.launch_count()
         with torch.cuda.graph(captured.graph):
             captured.logits = self.model(captured.ids, past_key_values=self.cache, use_cache=True, **kwargs).logits
+        captured.cache_kernels = _lib.launch_count() - launched
         captured.graph.replay()
         self._captured = captured
         return captured.logits

@@ -199,11 +199,6 @@ class OpBench:
         self.plan = _lib.plan(_lib.OP_FUSED_STEP, batch, HKV, HQ, D, torch.float32, bf, slots + 1,
                               N_SINK, self.window, 1, sms)
 
-    def launches_per_step(self) -> int:
-        if self.plan["splits"] == 1 or self.plan["cluster_ctas"] > 1:
-            return 1  # one split, or every split of a pair in one cluster: a single launch
-        return 3  # halo pre-pass, stream kernel, split combine
-
     def step(self, i: int) -> None:
         j = i % self.POOL
         self.lib.fused_decode_step(self.k, self.v, self.kn[j], self.vn[j], self.q[j], N_SINK, self.window, 1,
@@ -219,7 +214,8 @@ class OpBenchV2:
     n_sink region rows (original keys at positions 0..n_sink-1), the device position far
     from the origin, plus a small pool of per-step inputs.  A step is sink_v2_decode_step:
     the place kernel (ring write, region rotation, position advance), split-K attention over
-    the window + 1 + n_sink rows and the split combine."""
+    the window + 1 + n_sink rows and the split combine (the place work runs inside the
+    tensor-core attention kernel when there are no more pairs than SMs)."""
 
     POOL = 4
 
@@ -250,9 +246,6 @@ class OpBenchV2:
         sms = _lib.sm_count(device)
         self.ws.get(_lib.workspace_bytes(_lib.OP_ATTEND, batch, HKV, HQ, D, bf, bf, self.rows, 0, 1, 0, sms), device)
         self.plan = _lib.plan(_lib.OP_ATTEND, batch, HKV, HQ, D, bf, bf, self.rows, 0, 1, 0, sms)
-
-    def launches_per_step(self) -> int:
-        return 2 + (1 if self.plan["splits"] > 1 else 0)  # place, attention, split combine
 
     def step(self, i: int) -> None:
         j = i % self.POOL
@@ -554,7 +547,7 @@ def sweep(device: torch.device, flush: torch.Tensor, cls=None, alg=None) -> dict
             row = {"us_per_layer": round(ms * 1e3, 2), "GB_s": round(alg(slots) * batch / (ms * 1e-3) / 1e9, 1),
                    "l2_flushed": small}
             if small:
-                n = min(64, max(2, math.ceil(2.5 * L2_BYTES / b.state_bytes())))
+                n = min(320, max(2, math.ceil(2.5 * L2_BYTES / b.state_bytes())))
                 layers = [b] + [cls(batch, slots, device, seed=slots + batch + 97 * i) for i in range(1, n)]
                 ms_seq = time_graph_layers(layers)
                 row["us_per_layer_in_sequence"] = round(ms_seq * 1e3, 2)
@@ -719,9 +712,9 @@ class ModelBench:
                    for l in self.cache.layers)
 
     def step_kernels(self) -> int:
-        """Sink-cache kernels per decode step: v1 halo + stream + combine, v2 place + attention
-        + combine, per layer (an upper bound when a layer's plan has a single split)."""
-        return 3 * self.cfg.num_hidden_layers
+        """Sink-cache kernels per decode step: those the library launched while the replayed
+        step was captured."""
+        return self.runner.cache_kernels_per_replay
 
 
 def stream_run(spec: dict, stream_ids: list[int], device: torch.device, steps: int, warmup: int,
@@ -954,7 +947,7 @@ def main():
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    from attention_sinks_b200 import build
+    from attention_sinks_b200 import _lib, build
     build.build()  # no-op when the shipped library is current
 
     bench = kind["cls"](args.streams, args.slots, device, seed=1000 + rank)
@@ -970,7 +963,9 @@ def main():
     torch.cuda.synchronize()
     clocks = ClockSampler(device)
     clocks.start()
+    n_launched = _lib.launch_count()
     ms = time_device(bench, args.steps, 0, l2_flush)
+    launches = _lib.launch_count() - n_launched  # the library's kernels in the timed region
     clk = clocks.stop()
     torch.cuda.synchronize()
     streams.barrier()
@@ -1002,7 +997,6 @@ def main():
     if "traffic_workload" in prof:
         roofline["traffic_workload"] = prof["traffic_workload"]
 
-    launches = bench.launches_per_step() * args.steps
     plan = dict(bench.plan)
     del bench
     torch.cuda.empty_cache()

@@ -91,6 +91,14 @@ typedef struct sink_rows {
 /* Library ABI version (SINK_ABI_VERSION). */
 int32_t sink_abi_version(void);
 
+/*
+ * Kernel launches this library has issued in the calling process so far (every successful
+ * launch of every entry point; replays of a CUDA graph that captured them are not counted).
+ * For benchmarks and tests: the difference across a region is the number of this library's
+ * kernels launched inside it.  No counterpart in the reference.
+ */
+uint64_t sink_launch_count(void);
+
 /* Human-readable text for any return code of this library (negative or cudaError_t). */
 const char* sink_strerror(int32_t code);
 
@@ -266,7 +274,10 @@ int32_t sink_v2_place(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
  * step with (k_new, v_new) and `position`, then decode attention of q [batch, heads_q, 1,
  * head_dim] over the window + 1 + R rows (ring, then region) -- as sink_decode_attention,
  * with its mask convention over those rows.  Workspace: sink_workspace_bytes(SINK_OP_ATTEND,
- * ..., rows = window + 1 + R, ...).  Replaces SinkLayerV2._decode_step (cache_v2.py:167-181)
+ * ..., rows = window + 1 + R, ...).  On the tensor-core path (16-bit K and V, head_dim 128)
+ * the place work runs inside the attention kernel, each CTA on the rows of its own split
+ * items, so the step is one launch (plus the split combine when the splits do not fit one
+ * cluster each); otherwise the place kernel runs first.  Replaces SinkLayerV2._decode_step (cache_v2.py:167-181)
  * followed by decode_attention_forward over the views it returns (decode_attention.py:136-143).
  */
 int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
@@ -292,6 +303,16 @@ int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_ne
  * attention leaves them untouched).  Returns 0, or SINK_EINVAL for chunk < 0 or polls < 1.
  */
 int32_t sink_debug_fail_next_wait(int32_t chunk, int32_t polls);
+
+/*
+ * Test hook for the cluster fallback: clusters >= 0 is taken as the number of clusters the
+ * device can hold at once for every clustered stream launch of the process (0: none can be
+ * placed, so clustered plans run as split launches -- halo pre-pass, stream kernel, combine
+ * -- with the same splits); -1 (the default) asks the device (cudaOccupancyMaxActiveClusters,
+ * once per kernel and cluster size, outside stream capture).  Launches nothing.  Returns 0,
+ * or SINK_EINVAL for clusters < -1.
+ */
+int32_t sink_debug_cluster_capacity(int32_t clusters);
 
 /*
  * The rows a ring-buffer layer's multi-token step attends over, in the reference's order

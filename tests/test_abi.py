@@ -100,9 +100,10 @@ def test_plan_covers_rows_exactly(op, rows, n_sink, window, drop, batch, kdt):
 ])
 def test_plan_clusters_small_steps(batch, slots, ns, mode, built_lib):
     """Fused steps whose CTAs fit one wave with at most 16 splits per pair (or 16 splits
-    that add at most 4 chunks per split) run as one clustered launch: no halo or partials
-    workspace.  Clusters of more than 8 CTAs only for splits of at most 4 chunks.  Several
-    waves, or longer splits, keep the split launch with its halo pre-pass and combine."""
+    that add at most 4 chunks per split) run as one clustered launch.  Clusters of more than
+    8 CTAs only for splits of at most 4 chunks.  Several waves, or longer splits, keep the
+    split launch with its halo pre-pass and combine.  Every split plan, clustered or not,
+    has the split launch's partials and halo rows in its workspace."""
     f32, bf16 = torch.float32, torch.bfloat16
     args = (_lib.OP_FUSED_STEP, batch, 8, 16, 128, f32, bf16, slots + 1, 4, slots - 4, 1, 148)
     p = _lib.plan(*args)
@@ -110,7 +111,11 @@ def test_plan_clusters_small_steps(batch, slots, ns, mode, built_lib):
     want = {"split": _lib.LAUNCH_SPLIT, "cluster": _lib.LAUNCH_CLUSTER}[mode]
     assert p["splits"] == ns and p["cluster_ctas"] == (ns if clustered else 1) and p["launch"] == want
     ws = _lib.workspace_bytes(*args)
-    assert (ws == 256) == (clustered or ns == 1)  # the status word alone
+    assert (ws == 256) == (ns == 1)  # the status word alone
+    if clustered:  # the same plan split: partials of O, m, l and one halo row per split
+        parts = batch * 8 * ns * 2
+        halo = batch * 8 * ns * 128 * (4 + 2)
+        assert ws >= 256 + parts * 128 * 4 + 2 * parts * 4 + halo
     # a shift of more than 4 rows, or 16-bit K attention on the tensor cores, is never clustered
     assert _lib.plan(_lib.OP_EVICT, batch, 8, 8, 128, f32, bf16, 0, 4, slots - 4, 5, 148)["cluster_ctas"] == 1
     assert _lib.plan(_lib.OP_ATTEND, batch, 8, 16, 128, bf16, bf16, slots, 0, 1, 0, 148)["cluster_ctas"] == 1

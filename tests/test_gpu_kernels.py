@@ -228,6 +228,58 @@ def test_fused_equals_unfused(built_lib):
     torch.testing.assert_close(oa, ob, rtol=0, atol=0)
 
 
+@pytest.mark.parametrize("op,drop,launches", [("fused", 1, 3), ("fused", 3, 3), ("evict", 2, 2), ("attend", 0, 2)])
+def test_cluster_fallback_runs_the_plan_split(op, drop, launches, built_lib):
+    """A clustered plan (one stream, 1,024 slots: clusters of 11 or 16 CTAs) on a device that
+    cannot place the cluster runs the same splits as a split launch -- halo pre-pass (when
+    the window shifts), stream kernel, combine (when it attends) -- with the cache left bit
+    for bit as the clustered launch leaves it and outputs equal within 1e-2."""
+    g = torch.Generator().manual_seed(11 + drop)
+    b, hkv, hq, d, n_sink, window = 1, 8, 16, 128, 4, 1020
+    inv = cases.inv_freq(d, 1e6)
+    k = (torch.randn(b, hkv, n_sink + window + 4, d, generator=g) * 5).to(DEV)
+    v = torch.randn(b, hkv, n_sink + window + 4, d, generator=g).bfloat16().to(DEV)
+    k1 = torch.randn(b, hkv, 1, d, generator=g).bfloat16().to(DEV)
+    v1 = torch.randn(b, hkv, 1, d, generator=g).bfloat16().to(DEV)
+    q = torch.randn(b, hq, 1, d, generator=g).bfloat16().to(DEV)
+    cos, sin = [t.to(DEV) for t in oracle.rope_cos_sin(torch.tensor(-drop), inv)]
+    f32, bf = torch.float32, torch.bfloat16
+    plans = {"fused": (_lib.OP_FUSED_STEP, hq, n_sink + window + 1), "evict": (_lib.OP_EVICT, hkv, 0),
+             "attend": (_lib.OP_ATTEND, hq, n_sink + window)}
+    code, heads_q, rows = plans[op]
+    p = _lib.plan(code, b, hkv, heads_q, d, f32, bf, rows, n_sink, window, drop, _lib.sm_count(torch.device(DEV)))
+    assert p["cluster_ctas"] > 1
+
+    def run(capacity):
+        kk, vv = k.clone(), v.clone()
+        out = torch.zeros(b, 1, hq, d, dtype=bf, device=DEV)
+        ws = _lib.Workspace()
+        _lib.force_cluster_capacity(capacity)
+        try:
+            torch.cuda.synchronize()
+            n0 = _lib.launch_count()
+            if op == "fused":
+                _lib.fused_decode_step(kk, vv, k1, v1, q, n_sink, window, drop, n_sink + window, cos, sin,
+                                       d ** -0.5, out, ws)
+            elif op == "evict":
+                _lib.evict_rerotate(kk, vv, n_sink, window, drop, cos, sin, ws)
+            else:
+                _lib.decode_attention(q, kk, vv, rows, d ** -0.5, out, ws)
+            n = _lib.launch_count() - n0
+            torch.cuda.synchronize()
+        finally:
+            _lib.force_cluster_capacity(-1)
+        _status_clean(ws)
+        return kk, vv, out, n
+
+    ka, va, oa, na = run(-1)
+    kb, vb, ob, nb = run(0)
+    assert (na, nb) == (1, launches)
+    torch.testing.assert_close(ka, kb, rtol=0, atol=0)
+    torch.testing.assert_close(va, vb, rtol=0, atol=0)
+    torch.testing.assert_close(oa.float(), ob.float(), rtol=0, atol=1e-2)
+
+
 def _masked_oracle(q, k, v, mask, scale):
     """Attention per stream over the rows its boolean mask keeps."""
     outs = []

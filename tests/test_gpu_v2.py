@@ -82,11 +82,17 @@ def test_place_step_matches_oracle(dtype, d, rot, t):
 
 @pytest.mark.parametrize("batch,hq,hkv,d,window,R", [
     (1, 16, 8, 128, 1020, 4), (4, 32, 8, 64, 300, 0), (2, 14, 2, 128, 4095, 36), (3, 8, 8, 256, 60, 1),
-    (1, 16, 8, 128, 32764, 4),
+    (1, 16, 8, 128, 32764, 4), (32, 16, 8, 128, 4095, 4), (8, 64, 8, 128, 1020, 4),
+    (8, 16, 8, 128, 32764, 4), (18, 16, 8, 128, 2047, 4), (19, 16, 8, 128, 2047, 4),
 ])
 def test_fused_decode_step_matches_place_then_attention(batch, hq, hkv, d, window, R):
     """sink_v2_decode_step leaves the cache exactly as sink_v2_place does, and its
-    attention over ring + region is within 2e-2 of fp32 attention over the same rows."""
+    attention over ring + region is within 2e-2 of fp32 attention over the same rows: with
+    the place work inside the tensor-core kernel (16-bit head_dim 128, pairs <= SMs and at
+    most 32 chunks of 128 rows per SM: 18 x 8 = 144 pairs) and on the place kernel before it
+    (19 x 8 = 152 pairs; 8 x 8 at 32,768 slots, a long step; the stream kernel at head_dim
+    64 and 256).  The launch count tells which ran: the step launches what attention over
+    the same rows launches, plus the place kernel where it is not fused."""
     g = torch.Generator().manual_seed(window + R)
     ring, dt = window + 1, torch.bfloat16
     t = 5 * window + 13
@@ -102,10 +108,19 @@ def test_fused_decode_step_matches_place_then_attention(batch, hq, hkv, d, windo
     pos = torch.tensor([t, 0], device=DEV)
     out = torch.empty(batch, 1, hq, d, dtype=dt, device=DEV)
     ws = _lib.Workspace()
+    n0 = _lib.launch_count()
     _lib.v2_decode_step(kbuf, vbuf, k, v, reg_k, reg_pos, R, pos, 4, window, inv, q, d ** -0.5, out, ws)
+    n_step = _lib.launch_count() - n0
     assert pos.tolist() == ref_pos.tolist() == [t + 1, 0]
     assert torch.equal(kbuf, ref_k) and torch.equal(vbuf, ref_v)
     rows = ring + R
+    n0 = _lib.launch_count()
+    _lib.decode_attention(q, ref_k, ref_v, rows, d ** -0.5, torch.empty_like(out), _lib.Workspace())
+    n_attend = _lib.launch_count() - n0
+    sms = _lib.sm_count(torch.device(DEV))
+    pairs = batch * hkv
+    fused = d == 128 and pairs <= sms and pairs * -(-rows // 128) <= 32 * sms
+    assert n_step == n_attend + (0 if fused else 1)
     want = oracle.decode_attention(q.cpu(), ref_k[:, :, :rows].cpu(), ref_v[:, :, :rows].cpu(), d ** -0.5)
     torch.testing.assert_close(out.float().cpu(), want, rtol=0, atol=2e-2)
     assert ws.read_status() == 0

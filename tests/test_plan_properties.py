@@ -3,7 +3,8 @@ through the C ABI, no GPU) over random shapes: the splits tile each (batch, head
 rows exactly; a clustered single-launch plan respects the limits its kernel relies on (at
 most 16 CTAs, every CTA in one wave, a shift of at most 4 rows, clusters above 8 CTAs only
 for splits of at most 4 chunks, never for the tensor-core attention); and the workspace
-holds exactly what the chosen regime uses."""
+holds what the split launch of the plan uses, clustered or not (a device that cannot place
+the cluster runs the same plan split)."""
 
 import pytest
 import torch
@@ -67,7 +68,7 @@ def test_plan_invariants(built_lib, args):
         assert p["launch"] == _lib.LAUNCH_SPLIT and p["ctas"] == pairs * ns
     ws = _lib.workspace_bytes(*args)
     attends = op != _lib.OP_EVICT
-    if ctas > 1 or ns == 1:
+    if ns == 1:
         assert ws == 256  # the status word alone: no partials, no halo rows
     else:
         need = 256
