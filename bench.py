@@ -343,32 +343,55 @@ def run_e2e(bench: OpBench, steps: int, warmup: int) -> tuple[float, int, int]:
     return start.elapsed_time(end) / steps, h2d, d2h
 
 
-def cpu_baseline(slots: int, seconds: float = 15.0) -> dict:
-    """The reference's CPU path (oracle port: SinkLayer.update on the PyTorch branch + SDPA
-    attention) on this host's cores, for one stream of the workload, as many steps as fit
-    in about `seconds`."""
-    import oracle
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    layer = oracle.make_prefilled_cache(1, HKV, D, slots, N_SINK, inv_freq(), seed=0)
-    g = torch.Generator().manual_seed(1)
-    q = torch.randn(1, HQ, 1, D, generator=g).bfloat16()
-    kn = torch.randn(1, HKV, 1, D, generator=g).bfloat16()
-    vn = torch.randn(1, HKV, 1, D, generator=g).bfloat16()
-    oracle.reference_cpu_step(layer, q, kn, vn, D ** -0.5)  # warm-up
+def cpu_streams(streams: int, state_bytes_per_stream: int) -> int:
+    """Streams the CPU baseline holds at once: the workload's, unless five copies of that
+    state (the buffers and the step's temporaries) would not fit this host's memory."""
+    try:
+        ram = os.sysconf("SC_PAGE_SIZE") * os.sysconf("SC_PHYS_PAGES")
+    except (ValueError, OSError):
+        return 1
+    n = streams
+    while n > 1 and 5 * n * state_bytes_per_stream > ram:
+        n //= 2
+    return n
+
+
+def _time_cpu_steps(step, seconds: float) -> tuple[float, int]:
+    """ms per step of `step()` after one warm-up call: as many calls as fit in `seconds` (at
+    least one)."""
+    step()
     n, t0 = 0, time.perf_counter()
     while True:
-        oracle.reference_cpu_step(layer, q, kn, vn, D ** -0.5)
+        step()
         n += 1
         el = time.perf_counter() - t0
         if el > seconds or n >= 1000:
-            break
-    ms = el * 1e3 / n
-    return {"value": round(alg_bytes(slots) / (ms * 1e-3) / 1e9, 3), "unit": "GB/s", "cores": threads,
-            "kind": "port", "ms_per_step": round(ms, 3),
-            "sample": f"1 stream x {slots} slots (of the per-GPU workload), {n} steps, oracle port of "
-                      f"SinkLayer.update (PyTorch path) + SDPA, torch threads={threads}; taken as the rate of "
-                      f"the whole batch, whose work is linear in the streams (not timed at 64 streams)"}
+            return el * 1e3 / n, n
+
+
+def cpu_baseline(slots: int, seconds: float = 15.0, streams: int = 1) -> dict:
+    """The reference's CPU path (oracle port: SinkLayer.update on the PyTorch branch + SDPA
+    attention) on this host's cores over the workload's streams as one batch, as many steps
+    as fit in about `seconds`.  One stream's state is built and repeated over the batch (a
+    step's work does not depend on the values)."""
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    n_streams = cpu_streams(streams, (slots + 1) * HKV * D * (4 + 2))
+    layer = oracle.make_prefilled_cache(1, HKV, D, slots, N_SINK, inv_freq(), seed=0)
+    layer.kbuf, layer.vbuf = layer.kbuf.repeat(n_streams, 1, 1, 1), layer.vbuf.repeat(n_streams, 1, 1, 1)
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(n_streams, HQ, 1, D, generator=g).bfloat16()
+    kn = torch.randn(n_streams, HKV, 1, D, generator=g).bfloat16()
+    vn = torch.randn(n_streams, HKV, 1, D, generator=g).bfloat16()
+    ms, n = _time_cpu_steps(lambda: oracle.reference_cpu_step(layer, q, kn, vn, D ** -0.5), seconds)
+    del layer
+    rate = alg_bytes(slots) * n_streams / (ms * 1e-3) / 1e9
+    scaled = "" if n_streams == streams else f"; host memory held {n_streams} of the {streams} streams, rate taken for all"
+    return {"value": round(rate, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "ms_per_step": round(ms * streams / n_streams, 3),
+            "sample": f"{n_streams} streams x {slots} slots as one batch, {n} steps after a warm-up, oracle port "
+                      f"of SinkLayer.update (PyTorch path) + SDPA, torch threads={threads}{scaled}"}
 
 
 def run_e2e_v2(bench: OpBenchV2, steps: int, warmup: int) -> tuple[float, int, int]:
@@ -413,31 +436,29 @@ def run_e2e_v2(bench: OpBenchV2, steps: int, warmup: int) -> tuple[float, int, i
     return start.elapsed_time(end) / steps, h2d, d2h
 
 
-def cpu_baseline_v2(slots: int, seconds: float = 15.0) -> dict:
+def cpu_baseline_v2(slots: int, seconds: float = 15.0, streams: int = 1) -> dict:
     """The reference's CPU path for the ring-buffer layer (oracle port: SinkLayerV2.update +
-    SDPA attention) on this host's cores, one stream of the workload."""
+    SDPA attention) on this host's cores over the workload's streams as one batch (one
+    stream's state repeated)."""
     import oracle
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
+    n_streams = cpu_streams(streams, (slots + N_SINK) * HKV * D * 4)
     layer = oracle.make_prefilled_cache_v2(1, HKV, D, slots, N_SINK, inv_freq(), seed=0)
+    for name in ("kbuf", "vbuf", "reg_k"):
+        setattr(layer, name, getattr(layer, name).repeat(n_streams, 1, 1, 1))
     g = torch.Generator().manual_seed(1)
-    q = torch.randn(1, HQ, 1, D, generator=g).bfloat16()
-    kn = torch.randn(1, HKV, 1, D, generator=g).bfloat16()
-    vn = torch.randn(1, HKV, 1, D, generator=g).bfloat16()
-    oracle.reference_cpu_step_v2(layer, q, kn, vn, D ** -0.5)  # warm-up
-    n, t0 = 0, time.perf_counter()
-    while True:
-        oracle.reference_cpu_step_v2(layer, q, kn, vn, D ** -0.5)
-        n += 1
-        el = time.perf_counter() - t0
-        if el > seconds or n >= 1000:
-            break
-    ms = el * 1e3 / n
-    return {"value": round(alg_bytes_v2(slots) / (ms * 1e-3) / 1e9, 3), "unit": "GB/s", "cores": threads,
-            "kind": "port", "ms_per_step": round(ms, 3),
-            "sample": f"1 stream x {slots} slots (of the per-GPU workload), {n} steps, oracle port of "
-                      f"SinkLayerV2.update (ring step) + SDPA, torch threads={threads}; taken as the rate of "
-                      f"the whole batch, whose work is linear in the streams (not timed at 64 streams)"}
+    q = torch.randn(n_streams, HQ, 1, D, generator=g).bfloat16()
+    kn = torch.randn(n_streams, HKV, 1, D, generator=g).bfloat16()
+    vn = torch.randn(n_streams, HKV, 1, D, generator=g).bfloat16()
+    ms, n = _time_cpu_steps(lambda: oracle.reference_cpu_step_v2(layer, q, kn, vn, D ** -0.5), seconds)
+    del layer
+    rate = alg_bytes_v2(slots) * n_streams / (ms * 1e-3) / 1e9
+    scaled = "" if n_streams == streams else f"; host memory held {n_streams} of the {streams} streams, rate taken for all"
+    return {"value": round(rate, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "ms_per_step": round(ms * streams / n_streams, 3),
+            "sample": f"{n_streams} streams x {slots} slots as one batch, {n} steps after a warm-up, oracle port "
+                      f"of SinkLayerV2.update (ring step) + SDPA, torch threads={threads}{scaled}"}
 
 
 def time_graph(bench: OpBench, steps: int, flush: torch.Tensor | None) -> float:
@@ -932,7 +953,7 @@ def main():
             return
         steps = max(1, args.steps)
         seconds = min(120.0, 0.3 * steps + 5)
-        cb = kind["cpu"](args.slots, seconds=seconds)
+        cb = kind["cpu"](args.slots, seconds=seconds, streams=args.streams)
         v = cb["value"] * 1.0
         line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_step"],
@@ -1009,7 +1030,7 @@ def main():
             del flush
             torch.cuda.empty_cache()
         if not args.no_cpu:
-            extra["cpu_baseline"] = kind["cpu"](args.slots)
+            extra["cpu_baseline"] = kind["cpu"](args.slots, streams=args.streams)
     if not args.no_model:  # every rank: per-rank NLL sums and times are gathered over NCCL
         extra["model"] = model_leg(device, rank, world, args.model_steps, args.warmup)
     if rank == 0:

@@ -163,10 +163,13 @@ def test_fused_step_matches_reference(spec, golden, golden_arrays, built_lib):
 
 @pytest.mark.parametrize("batch,hq,hkv,d,n_sink,window,steps", [
     (2, 16, 8, 128, 4, 60, 90), (1, 32, 8, 64, 4, 1020, 40), (3, 16, 8, 128, 0, 33, 50),
+    (1, 16, 8, 128, 4, 1020, 12),
 ])
 def test_fused_stream_matches_oracle(batch, hq, hkv, d, n_sink, window, steps, built_lib):
     """Many fused steps in a row, filling the cache and then evicting every step, against
-    the oracle fed the same tokens: cache bit-exact at every step, outputs within 2e-2."""
+    the oracle fed the same tokens: cache bit-exact at every step, outputs within 2e-2.
+    One stream at 1,024 slots passes through clustered tail plans (the appended row merged
+    as its own partial and written by the last split) while it fills and when it evicts."""
     g = torch.Generator().manual_seed(11)
     inv = cases.inv_freq(d, 1e6)
     cap = n_sink + window
@@ -201,11 +204,19 @@ def test_fused_stream_matches_oracle(batch, hq, hkv, d, n_sink, window, steps, b
     _status_clean(ws)
 
 
-def test_fused_equals_unfused(built_lib):
+@pytest.mark.parametrize("b,window,launch", [(4, 2044, _lib.LAUNCH_SPLIT), (1, 1020, _lib.LAUNCH_CLUSTER_TAIL),
+                                              (8, 252, _lib.LAUNCH_CLUSTER_TAIL)])
+def test_fused_equals_unfused(b, window, launch, built_lib):
     """The fused step leaves the cache bit-identical to evict + append, and its output equals
-    decode attention over the updated cache."""
+    decode attention over the updated cache -- bit for bit, with both on the split launch
+    and with both on the clustered tail plan (the appended row merged as its own partial
+    in the fused step, the last cached row in the attention)."""
     g = torch.Generator().manual_seed(5)
-    b, hkv, hq, d, n_sink, window = 4, 8, 16, 128, 4, 2044
+    hkv, hq, d, n_sink = 8, 16, 128, 4
+    sms = _lib.sm_count(torch.device(DEV))
+    for op, rows, drop in ((_lib.OP_FUSED_STEP, n_sink + window + 1, 1), (_lib.OP_ATTEND, n_sink + window + 1, 0)):
+        p = _lib.plan(op, b, hkv, hq, d, torch.float32, torch.bfloat16, rows, n_sink, window, drop, sms)
+        assert p["launch"] == launch
     inv = cases.inv_freq(d, 1e6)
     k = (torch.randn(b, hkv, n_sink + window + 1, d, generator=g) * 5).to(DEV)
     v = torch.randn(b, hkv, n_sink + window + 1, d, generator=g).bfloat16().to(DEV)
