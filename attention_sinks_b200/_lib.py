@@ -27,7 +27,7 @@ EXPORTED_SYMBOLS = (
     "sink_debug_fail_next_wait", "sink_plan_launch", "sink_evict_rerotate_keycopy", "sink_v2_gather",
     "sink_debug_cluster_capacity", "sink_launch_count",
 )
-LAUNCH_SPLIT, LAUNCH_CLUSTER, LAUNCH_TENSOR, LAUNCH_CLUSTER_TAIL = 0, 1, 2, 3
+LAUNCH_SPLIT, LAUNCH_CLUSTER, LAUNCH_TENSOR = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 16 << 20
 # argument errors (negative return codes of the C ABI)
 EINVAL, EDTYPE, EHEADDIM, EGROUP, ELAYOUT, EWORKSPACE, EDEVICE, ESCRATCH = -1, -2, -3, -4, -5, -6, -7, -8

@@ -76,12 +76,6 @@ struct StreamArgs {
   // and head km_sb / km_sh, rows contiguous).  NULL: none.
   char* kmirror;
   int64_t km_sb, km_sh;
-  // 1 (clustered attention only): row `row_end` -- the appended token of a fused step, or
-  // the last cached row of an attention -- is left out of the splits and merged as one more
-  // partial in the cluster merge (score, weight 1, value), so that ns splits of rows
-  // [row_begin, row_end) need not spend a chunk on one row.  A fused step's CTA of the last
-  // split writes the appended row after its loads.
-  int tail;
 };
 
 // Rows [a, e) of split j.
@@ -359,15 +353,11 @@ __host__ __device__ constexpr int merge_scratch_bytes(int warps, int groups, int
   return warps * groups * (D + 2) * 4;
 }
 
-// Partials a cluster merge weighs per query row: the ns <= kClusterMax splits and the tail row.
-constexpr int kMergeSlots = kClusterMax + 1;
-
 // Floats of a clustered launch's merge area: the pair's G * D outputs split into ns equal
 // slices, one slice per CTA, each received from every CTA (ns * ceil(G * D / ns) <=
-// G * D + ns - 1 floats), then every CTA's (M, L) per group, the merge weights, and the
-// tail row's score per group.
+// G * D + ns - 1 floats), then every CTA's (M, L) per group, and the merge weights.
 __host__ __device__ constexpr int cluster_merge_floats(int groups, int D) {
-  return groups * D + kClusterMax + 3 * groups * kMergeSlots + groups;
+  return groups * D + kClusterMax + 3 * groups * kClusterMax;
 }
 
 // Compile-time geometry of the stream kernel for one (K type, V type, head_dim).

@@ -111,13 +111,6 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
   unsigned char* stages = smem + kBarrierBytes;
   unsigned char* halo_sk = stages + S * STAGE;  // clustered: this split's halo rows
   unsigned char* halo_sv = halo_sk + kClusterHaloRows * KROW;
-  // clustered: the merge area after the halo rows -- received outputs [ns][per], (M, L) and
-  // weights [GMAX][kMergeSlots] each, the tail row's scores [GMAX]
-  float* recv_o = reinterpret_cast<float*>(halo_sv + kClusterHaloRows * VROW);
-  float* recv_m = recv_o + GMAX * D + kClusterMax;
-  float* recv_l = recv_m + GMAX * kMergeSlots;
-  float* wts = recv_l + GMAX * kMergeSlots;
-  float* tail_s = wts + GMAX * kMergeSlots;
   const uint32_t halo_bar = bar0 + 8 * S;
   const bool clustered = A.cluster != 0;  // grid-uniform
 
@@ -183,50 +176,6 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
   L.init(A);
   L.begin_pair(A, b, h);
   const uint8_t* mrow = A.mask != nullptr ? A.mask + b * A.mask_sb : nullptr;
-
-  // Tail plan (clustered attention): the last row's scores and this CTA's first value of it
-  // are read now, while the first chunks are in flight, so the merge waits on no load.
-  float vtail0 = 0.f;
-  if constexpr (ATTEND) {
-    if (A.tail) {
-      const int trow = A.row_end;
-      if (tid < 32) {
-        // formed as L.chunk forms a row's score (same lanes, same order); the key is the
-        // appended token rounded through the key type, or the cached row
-        float lo[4], hi[4];
-        if (A.append_row >= 0) {
-          const VT* kn = reinterpret_cast<const VT*>(A.knew) + b * A.kn_sb + h * A.kn_sh;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            lo[i] = Elem<KT>::round(Elem<VT>::to_f(kn[4 * L.li + i]));
-            hi[i] = Elem<KT>::round(Elem<VT>::to_f(kn[D / 2 + 4 * L.li + i]));
-          }
-        } else {
-          Elem<KT>::load4(kb + size_t(trow) * D + 4 * L.li, lo);
-          Elem<KT>::load4(kb + size_t(trow) * D + D / 2 + 4 * L.li, hi);
-        }
-        const bool seen = mrow == nullptr || mrow[trow] != 0;
-#pragma unroll
-        for (int g = 0; g < GMAX; ++g) {
-          float d = 0.f;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) d = __fmaf_rn(L.qlo[g][k], lo[k], d);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) d = __fmaf_rn(L.qhi[g][k], hi[k], d);
-#pragma unroll
-          for (int off = Lanes::LPR / 2; off >= 1; off >>= 1) d += __shfl_xor_sync(kFull, d, off);
-          if (tid == 0 && g < A.group) tail_s[g] = seen ? d : kNegInf;
-        }
-      }
-      const int G = A.group, per = (G * D + A.ns - 1) / A.ns;
-      const int idx = j * per + tid;
-      if (tid < per && idx < G * D) {
-        const VT* vt = A.append_row >= 0 ? reinterpret_cast<const VT*>(A.vnew) + b * A.vn_sb + h * A.vn_sh
-                                         : vb + size_t(trow) * D;
-        vtail0 = Elem<VT>::to_f(vt[idx % D]);
-      }
-    }
-  }
 
   bool failed = false, halo_landed = !halo_issued;
   if (clustered) {
@@ -301,18 +250,6 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
   }
   // A clustered CTA stays for the cluster barriers below (its results are void).
   if (failed && !clustered) return;
-  // Tail plan of a fused step: the last split has read the old row at append_row (a shift
-  // source) -- its loads have all landed -- so it now writes the appended token there.
-  if (A.tail && A.append_row >= 0 && j == A.ns - 1 && !failed) {
-    const VT* kn = reinterpret_cast<const VT*>(A.knew) + b * A.kn_sb + h * A.kn_sh;
-    const VT* vn = reinterpret_cast<const VT*>(A.vnew) + b * A.vn_sb + h * A.vn_sh;
-    for (int d = tid; d < D; d += NT) {
-      const float kx = Elem<VT>::to_f(kn[d]);
-      kb[size_t(A.append_row) * D + d] = Elem<KT>::from_f(kx);
-      vb[size_t(A.append_row) * D + d] = vn[d];
-      if (kmir != nullptr) kmir[size_t(A.append_row) * D + d] = Elem<VT>::from_f(Elem<KT>::round(kx));
-    }
-  }
 
   if constexpr (ATTEND) {
     float* scratch = reinterpret_cast<float*>(stages);
@@ -344,9 +281,11 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
     // after one cluster barrier each CTA merges its slice from its own shared memory.
     const int ns = A.ns;
     const int per = (G * D + ns - 1) / ns;
+    float* recv_o = reinterpret_cast<float*>(halo_sv + kClusterHaloRows * VROW);  // [ns][per]
+    float* recv_m = recv_o + GMAX * D + kClusterMax;                            // [GMAX][kClusterMax]
+    float* recv_l = recv_m + GMAX * kClusterMax;
+    float* wts = recv_l + GMAX * kClusterMax;
     const uint32_t o_addr = smem_addr(recv_o), m_addr = smem_addr(recv_m), l_addr = smem_addr(recv_l);
-    const bool tail = A.tail != 0;
-    const int trow = A.row_end;  // the tail row
     for (int idx = tid; idx < G * D; idx += NT) {
       const int g = idx / D, d = idx - g * D;
       float M, Ls, O;
@@ -355,37 +294,27 @@ __global__ void __launch_bounds__(32 * NW) sink_stream_kernel(const __grid_const
       st_cluster_f32(cluster_map(o_addr + 4u * uint32_t(j * per + idx - owner * per), uint32_t(owner)), O);
       if (d == 0) {
         for (int r = 0; r < ns; ++r) {
-          st_cluster_f32(cluster_map(m_addr + 4u * uint32_t(g * kMergeSlots + j), uint32_t(r)), M);
-          st_cluster_f32(cluster_map(l_addr + 4u * uint32_t(g * kMergeSlots + j), uint32_t(r)), Ls);
+          st_cluster_f32(cluster_map(m_addr + 4u * uint32_t(g * kClusterMax + j), uint32_t(r)), M);
+          st_cluster_f32(cluster_map(l_addr + 4u * uint32_t(g * kClusterMax + j), uint32_t(r)), Ls);
         }
       }
     }
     cluster_sync();  // every push has landed; after this no CTA touches another's memory
     if (!failed) {   // CTA-uniform
-      // normalised weights: one warp per group, one split per lane, the tail row after the
-      // splits (its partial: max = its score, sum 1, output its value row)
+      // normalised weights: one warp per group, one split per lane
       const int lane = tid & 31;
       for (int g = tid >> 5; g < G; g += NW) {
-        float mm = kNegInf, ll = 0.f;
-        if (lane < ns) {
-          mm = recv_m[g * kMergeSlots + lane];
-          ll = recv_l[g * kMergeSlots + lane];
-        } else if (tail && lane == ns) {
-          mm = tail_s[g];
-          ll = mm == kNegInf ? 0.f : 1.f;
-        }
-        const float w = split_weight(mm, ll);
-        if (lane < ns + (tail ? 1 : 0)) wts[g * kMergeSlots + lane] = w;
+        const bool live = lane < ns;
+        const float w = split_weight(live ? recv_m[g * kClusterMax + lane] : kNegInf,
+                                     live ? recv_l[g * kClusterMax + lane] : 0.f);
+        if (live) wts[g * kClusterMax + lane] = w;
       }
       __syncthreads();
-      const VT* vtail = A.append_row >= 0 ? reinterpret_cast<const VT*>(A.vnew) + b * A.vn_sb + h * A.vn_sh
-                                          : vb + size_t(trow) * D;
       const int lo = j * per, hi = imin(lo + per, G * D);
       for (int idx = lo + tid; idx < hi; idx += NT) {
         const int g = idx / D, d = idx - g * D, i = idx - lo;
         float o = 0.f;
-        for (int r = 0; r < ns; ++r) o = __fmaf_rn(wts[g * kMergeSlots + r], recv_o[r * per + i], o);
-        if (tail) o = __fmaf_rn(wts[g * kMergeSlots + ns], i == tid ? vtail0 : Elem<VT>::to_f(vtail[d]), o);
+        for (int r = 0; r < ns; ++r) o = __fmaf_rn(wts[g * kClusterMax + r], recv_o[r * per + i], o);
         VT* op = reinterpret_cast<VT*>(A.out) + b * A.o_sb + (h * G + g) * A.o_sh;
         op[d] = Elem<VT>::from_f(o);
       }

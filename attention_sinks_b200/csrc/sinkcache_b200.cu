@@ -40,7 +40,6 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 struct Plan {
   bool tc = false;       // attention on the tensor-core kernel (sink_attend_tc_kernel)
   bool cluster = false;  // stream kernel launched as one cluster of ns CTAs per pair
-  bool tail = false;     // clustered attention: the last row merged as a partial (StreamArgs::tail)
   int T = 0, S = 0, stage = 0, smem = 0, ctas_per_sm = 0;
   int ns = 1, rows_per_split = 0, halo_rows = 0;
   size_t off_o = 0, off_m = 0, off_l = 0, off_hk = 0, off_hv = 0, total = 256;
@@ -228,35 +227,15 @@ int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
   if (pl.tc)
     choose_splits(pairs, nrows, pl.T, num_sms, kTcTargetItemsPerCta, kTcMinItemChunks, false, pl);
   else {
-    const int slots = num_sms * pl.ctas_per_sm;
-    auto stream_plan = [&](int r, Plan& q) {
-      choose_splits(pairs, r, q.T, slots, kTargetWaves, kMinItemChunks, true, q);
-      if (drop > 0 && (op == SINK_OP_EVICT || op == SINK_OP_FUSED_STEP)) limit_halo(r, drop, q);
-      choose_cluster(pairs, r, q.T, slots, drop, q);
-    };
-    stream_plan(nrows, pl);
-    // A clustered attention over k chunks plus one row: with that row merged as a partial
-    // of its own (the tail), the splits cover k chunks, which may take a chunk off every
-    // split (1,025 rows: 16 splits of 2 chunks instead of 11 of 3).
-    if (attend && pl.cluster && nrows > 1 && (nrows - 1) % pl.T == 0) {
-      Plan t = pl;
-      t.ns = 1;
-      t.rows_per_split = 0;
-      t.cluster = false;
-      stream_plan(nrows - 1, t);
-      if (t.cluster && t.rows_per_split < pl.rows_per_split) {
-        pl = t;
-        pl.tail = true;
-      }
-    }
+    choose_splits(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, kTargetWaves, kMinItemChunks, true, pl);
+    if (drop > 0 && (op == SINK_OP_EVICT || op == SINK_OP_FUSED_STEP)) limit_halo(nrows, drop, pl);
+    choose_cluster(pairs, nrows, pl.T, num_sms * pl.ctas_per_sm, drop, pl);
   }
   // Partials and halo rows are reserved for clustered plans too: a device that cannot place
-  // the cluster runs the same splits as a split launch (settle_cluster), a tail plan with
-  // one more split for its last row.
-  const int ns_split = pl.tail ? (nrows + pl.rows_per_split - 1) / pl.rows_per_split : pl.ns;
+  // the cluster runs the same plan as a split launch (settle_cluster).
   size_t off = 256;  // status word
-  if (attend && ns_split > 1) {
-    const size_t parts = size_t(pairs) * ns_split * G;
+  if (attend && pl.ns > 1) {
+    const size_t parts = size_t(pairs) * pl.ns * G;
     pl.off_o = off;
     off += align256(parts * D * 4);
     pl.off_m = off;
@@ -265,9 +244,9 @@ int32_t make_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
     off += align256(parts * 4);
   }
   const bool evicts = op == SINK_OP_EVICT || op == SINK_OP_FUSED_STEP;
-  if (evicts && drop > 0 && ns_split > 1) {
+  if (evicts && drop > 0 && pl.ns > 1) {
     pl.halo_rows = drop < pl.rows_per_split ? drop : pl.rows_per_split;
-    const size_t hrows = size_t(pairs) * ns_split * pl.halo_rows;
+    const size_t hrows = size_t(pairs) * pl.ns * pl.halo_rows;
     pl.off_hk = off;
     off += align256(hrows * D * ks);
     pl.off_hv = off;
@@ -508,12 +487,6 @@ int32_t settle_cluster(const sink_kv_buffers_t* kv, int G, StreamArgs& A, Plan& 
   if (capacity < 1) {
     pl.cluster = false;
     A.cluster = 0;
-    if (pl.tail) {  // the tail row becomes a split of its own
-      pl.tail = false;
-      A.tail = 0;
-      A.row_end += 1;
-      pl.ns = A.ns = (A.row_end - A.row_begin + pl.rows_per_split - 1) / pl.rows_per_split;
-    }
   }
   return SINK_OK;
 }
@@ -583,7 +556,6 @@ void fill_common(StreamArgs& A, const sink_kv_buffers_t* kv, const Plan& pl, cha
   A.halo_k = pl.off_hk ? ws + pl.off_hk : nullptr;
   A.halo_v = pl.off_hv ? ws + pl.off_hv : nullptr;
   A.cluster = pl.cluster ? 1 : 0;
-  A.tail = pl.tail ? 1 : 0;
   A.wait_polls = kWaitPolls;
   A.skip_chunk = -1;
 }
@@ -783,7 +755,7 @@ int32_t launch_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int3
   A.o_sh = out_stride_h;
   A.window = 1;
   A.row_begin = 0;
-  A.row_end = rows - (pl.tail ? 1 : 0);
+  A.row_end = rows;
   A.written_end = 0;
   A.scale_log2 = scale * kLog2e;
   A.mask = mask;
@@ -1114,7 +1086,7 @@ int32_t sink_plan_launch(int32_t op, int32_t batch, int32_t heads_kv, int32_t he
     m = SINK_LAUNCH_TENSOR;
     n = items < num_sms ? items : num_sms;
   } else if (pl.cluster) {
-    m = pl.tail ? SINK_LAUNCH_CLUSTER_TAIL : SINK_LAUNCH_CLUSTER;
+    m = SINK_LAUNCH_CLUSTER;
   }
   if (op == SINK_OP_APPEND) n = 0;
   if (mode) *mode = m;
@@ -1280,7 +1252,7 @@ int32_t sink_fused_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k
   A.drop = drop;
   A.rotate = rotate ? 1 : 0;
   A.row_begin = 0;
-  A.row_end = append_row + 1 - (pl.tail ? 1 : 0);
+  A.row_end = append_row + 1;
   A.append_row = append_row;
   A.written_end = drop > 0 ? n_sink + window + 1 : append_row + 1;
   A.scale_log2 = scale * kLog2e;

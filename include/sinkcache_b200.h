@@ -130,8 +130,6 @@ int32_t sink_plan(int32_t op, int32_t batch, int32_t heads_kv, int32_t heads_q, 
 #define SINK_LAUNCH_SPLIT 0      /* one CTA per split; halo pre-pass and combine launches as needed */
 #define SINK_LAUNCH_CLUSTER 1    /* every split of a pair in one thread-block cluster: one launch */
 #define SINK_LAUNCH_TENSOR 2     /* the tensor-core attention kernel (16-bit K, head_dim 128) */
-#define SINK_LAUNCH_CLUSTER_TAIL 3  /* clustered; the splits cover rows - 1 and the last row (a
-                                       fused step's appended token) is merged as a partial of its own */
 
 /*
  * How the plan of sink_plan() is launched (for tests and profiling): *mode is one of

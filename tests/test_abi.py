@@ -73,8 +73,7 @@ def test_workspace_and_plan_are_host_arithmetic(built_lib):
 @pytest.mark.parametrize("kdt", [torch.float32, torch.bfloat16], ids=["k32", "k16"])
 def test_plan_covers_rows_exactly(op, rows, n_sink, window, drop, batch, kdt):
     """Splits tile each pair's rows with no gap and no empty split, in items of at most 32
-    chunks (8 or more, or one split per pair, when the step takes several waves); a tail plan
-    tiles all rows but the last, which the cluster merge takes.  16-bit K attention plans
+    chunks (8 or more, or one split per pair, when the step takes several waves).  16-bit K attention plans
     for the persistent tensor-core kernel: 128-row chunks, one CTA per SM, items of 2 or
     more chunks."""
     p = _lib.plan(op, batch, 8, 16, 128, kdt, torch.bfloat16, rows, n_sink, window, drop, 148)
@@ -87,16 +86,15 @@ def test_plan_covers_rows_exactly(op, rows, n_sink, window, drop, batch, kdt):
     assert rps % t == 0 and 1 <= ns <= 256 and rps <= max(32 * t, 6 * drop + 2 * t)
     if drop > 0 and ns > 1 and op != _lib.OP_ATTEND:
         assert rps >= 3 * drop
-    covered = total - 1 if p["launch"] == _lib.LAUNCH_CLUSTER_TAIL else total
-    assert (ns - 1) * rps < covered <= ns * rps
+    assert (ns - 1) * rps < total <= ns * rps
     slots = 148 * (233472 // (p["smem_bytes"] + 1024))  # CTA slots: SMs x CTAs per SM
     if batch * 8 * ns > slots:  # several waves: no more splits than items of 8 (tensor cores: 2) chunks give
         assert ns <= -(-(-(-total // t)) // (2 if t == 128 else 8))
 
 
 @pytest.mark.parametrize("batch,slots,ns,mode", [
-    (1, 256, 9, "cluster"), (1, 1024, 16, "tail"), (2, 2047, 16, "cluster"), (7, 4096, 5, "cluster"),
-    (8, 1024, 4, "tail"), (8, 256, 4, "tail"), (2, 4096, 17, "split"), (4, 4096, 9, "split"), (2, 8192, 18, "split"),
+    (1, 256, 9, "cluster"), (1, 1024, 11, "cluster"), (2, 2047, 16, "cluster"), (7, 4096, 5, "cluster"),
+    (8, 1024, 4, "cluster"), (2, 4096, 17, "split"), (4, 4096, 9, "split"), (2, 8192, 18, "split"),
     (4, 8192, 9, "split"), (1, 4096, 33, "split"), (64, 256, 1, "split"), (1, 32768, 37, "split"),
     (8, 4096, 9, "split"), (64, 32768, 33, "split"), (1, 16384, 37, "split"),
 ])
@@ -109,8 +107,8 @@ def test_plan_clusters_small_steps(batch, slots, ns, mode, built_lib):
     f32, bf16 = torch.float32, torch.bfloat16
     args = (_lib.OP_FUSED_STEP, batch, 8, 16, 128, f32, bf16, slots + 1, 4, slots - 4, 1, 148)
     p = _lib.plan(*args)
-    clustered = mode in ("cluster", "tail")
-    want = {"split": _lib.LAUNCH_SPLIT, "cluster": _lib.LAUNCH_CLUSTER, "tail": _lib.LAUNCH_CLUSTER_TAIL}[mode]
+    clustered = mode == "cluster"
+    want = {"split": _lib.LAUNCH_SPLIT, "cluster": _lib.LAUNCH_CLUSTER}[mode]
     assert p["splits"] == ns and p["cluster_ctas"] == (ns if clustered else 1) and p["launch"] == want
     ws = _lib.workspace_bytes(*args)
     assert (ws == 256) == (ns == 1)  # the status word alone

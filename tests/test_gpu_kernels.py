@@ -168,8 +168,7 @@ def test_fused_step_matches_reference(spec, golden, golden_arrays, built_lib):
 def test_fused_stream_matches_oracle(batch, hq, hkv, d, n_sink, window, steps, built_lib):
     """Many fused steps in a row, filling the cache and then evicting every step, against
     the oracle fed the same tokens: cache bit-exact at every step, outputs within 2e-2.
-    One stream at 1,024 slots passes through clustered tail plans (the appended row merged
-    as its own partial and written by the last split) while it fills and when it evicts."""
+    One stream at 1,024 slots runs clustered plans of every size while it fills."""
     g = torch.Generator().manual_seed(11)
     inv = cases.inv_freq(d, 1e6)
     cap = n_sink + window
@@ -204,13 +203,12 @@ def test_fused_stream_matches_oracle(batch, hq, hkv, d, n_sink, window, steps, b
     _status_clean(ws)
 
 
-@pytest.mark.parametrize("b,window,launch", [(4, 2044, _lib.LAUNCH_SPLIT), (1, 1020, _lib.LAUNCH_CLUSTER_TAIL),
-                                              (8, 252, _lib.LAUNCH_CLUSTER_TAIL)])
+@pytest.mark.parametrize("b,window,launch", [(4, 2044, _lib.LAUNCH_SPLIT), (1, 1020, _lib.LAUNCH_CLUSTER),
+                                              (8, 252, _lib.LAUNCH_CLUSTER)])
 def test_fused_equals_unfused(b, window, launch, built_lib):
     """The fused step leaves the cache bit-identical to evict + append, and its output equals
     decode attention over the updated cache -- bit for bit, with both on the split launch
-    and with both on the clustered tail plan (the appended row merged as its own partial
-    in the fused step, the last cached row in the attention)."""
+    (halo pre-pass, combine) and with both as one clustered launch (merge in the cluster)."""
     g = torch.Generator().manual_seed(5)
     hkv, hq, d, n_sink = 8, 16, 128, 4
     sms = _lib.sm_count(torch.device(DEV))

@@ -4,8 +4,7 @@ rows exactly; a clustered single-launch plan respects the limits its kernel reli
 most 16 CTAs, every CTA in one wave, a shift of at most 4 rows, clusters above 8 CTAs only
 for splits of at most 4 chunks, never for the tensor-core attention); and the workspace
 holds what the split launch of the plan uses, clustered or not (a device that cannot place
-the cluster runs the same plan split); a tail plan leaves exactly the last row to the
-cluster merge, where that row alone would have been a chunk."""
+the cluster runs the same plan split)."""
 
 import pytest
 import torch
@@ -44,18 +43,12 @@ def test_plan_invariants(built_lib, args):
     p = _lib.plan(*args)
     ns, rps, t, ctas = p["splits"], p["rows_per_split"], p["chunk_rows"], p["cluster_ctas"]
     total = window if op == _lib.OP_EVICT else rows
-    # a tail plan (clustered attention) leaves the last row to the cluster merge, and only
-    # where that row alone would have been a chunk
-    tail = p["launch"] == _lib.LAUNCH_CLUSTER_TAIL
-    if tail:
-        assert op != _lib.OP_EVICT and ctas > 1 and (total - 1) % t == 0
-    covered = total - 1 if tail else total
     # the splits tile the rows: no gap, no empty split, items of at most 32 chunks -- longer
     # only for a shift, whose splits stay 3 to 6 shifts long
     assert ns >= 1 and rps % t == 0 and rps <= max(32 * t, 6 * drop + 2 * t)
     if drop > 0 and ns > 1 and op != _lib.OP_ATTEND:
         assert rps >= 3 * drop
-    assert (ns - 1) * rps < covered <= ns * rps
+    assert (ns - 1) * rps < total <= ns * rps
     pairs = batch * hkv
     tensor_cores = t == 128 and p["stages"] == 3
     assert ctas in (1, ns)
@@ -68,7 +61,7 @@ def test_plan_invariants(built_lib, args):
     # the launch mode agrees with the plan: clusters of ns CTAs, or the tensor-core kernel's
     # persistent grid (one CTA per SM at most), or one CTA per split
     if ctas > 1:
-        assert p["launch"] in (_lib.LAUNCH_CLUSTER, _lib.LAUNCH_CLUSTER_TAIL) and p["ctas"] == pairs * ns
+        assert p["launch"] == _lib.LAUNCH_CLUSTER and p["ctas"] == pairs * ns
     elif tensor_cores:
         assert p["launch"] == _lib.LAUNCH_TENSOR and p["ctas"] == min(pairs * ns, sms)
     else:
@@ -79,8 +72,8 @@ def test_plan_invariants(built_lib, args):
         assert ws == 256  # the status word alone: no partials, no halo rows
     else:
         need = 256
-        if attends:  # the split partials of O (one more split for a tail plan run split)
-            need += pairs * (-(-total // rps) if tail else ns) * (hq // hkv) * d * 4
+        if attends:
+            need += pairs * ns * (hq // hkv) * d * 4  # the split partials of O
         assert ws >= need
 
 
