@@ -70,9 +70,13 @@ struct TcArgs {
   // 1: one item per CTA and the ns CTAs of each pair launched as one cluster; the pair's
   // split partials are merged at the end of the kernel (no sink_combine_kernel launch).
   int cluster;
-  // 1: the ring-buffer step's place work runs first, each CTA on the rows of its own items
-  // (no row belongs to two items), and the device position advances as in
-  // sink_v2_place_kernel: the v2 decode step in one launch.
+  // The ring-buffer step's place work in the same launch (the v2 decode step in one launch):
+  // each CTA places the rows of its own items (no row belongs to two items) and the device
+  // position advances as in sink_v2_place_kernel.  kTcPlaceFirst: every thread places
+  // before the pipeline starts (short steps; items split-major, so that the pairs' region
+  // and new-token items land on different CTAs).  kTcPlaceWarps: two warps place item by
+  // item beside the pipeline, which holds back only the chunks holding placed rows (long
+  // steps).  kTcPlaceNone: attention only.
   int place;
   V2PlaceArgs pa;
 };
@@ -198,18 +202,20 @@ __device__ __forceinline__ uint32_t tc_operand_offset(int r, int c) {
 
 // ------------------------------------------------------------------ kernel
 
+constexpr int kTcPlaceNone = 0, kTcPlaceFirst = 1, kTcPlaceWarps = 2;
+
 // Item `it` = (split j, pair p): its (batch, head), rows [a, e) and chunk count.  Pair-major
-// (it = p * ns + j), except with the place work fused in: split-major (it = j * pairs + p),
-// so that the pairs' items over the same rows -- the last split's region rows, the split
-// holding this step's ring slot -- are consecutive and land on different CTAs.  A clustered
-// launch (its clusters are the pairs) is always pair-major.
+// (it = p * ns + j); split-major (it = j * pairs + p) with kTcPlaceFirst, whose CTAs place
+// before they load: the pairs' items over the same rows -- the last split's region rows,
+// the split holding this step's ring slot -- are then consecutive and land on different
+// CTAs.  A clustered launch (its clusters are the pairs) is always pair-major.
 struct TcItem {
   int p, j, b, h, a, e, n;
 };
 
 __device__ __forceinline__ TcItem tc_item(const TcArgs& A, int it) {
   TcItem w;
-  if (A.cluster || !A.place) {
+  if (A.cluster || A.place != kTcPlaceFirst) {
     w.p = it / A.ns;
     w.j = it - w.p * A.ns;
   } else {
@@ -247,8 +253,32 @@ __device__ __forceinline__ void tc_load_q(const TcArgs& A, const TcItem& w, unsi
 // Warp roles: warps 0-3 run the softmax and the epilogues (thread i <-> TMEM lane i), warp 4
 // issues the MMAs, warp 5 issues the TMA loads.  They hand work to each other through
 // mbarriers only, so loads run up to three chunks ahead and MMA issue overlaps the softmax.
-constexpr int kTcThreads = 192;
-constexpr int kTcMmaWarp = 4, kTcLoadWarp = 5;
+// Warps 6-7 do the ring-buffer step's place work under kTcPlaceWarps and publish their
+// progress through release/acquire flags in shared memory; the load warp holds back only
+// the chunks that contain rows they write.
+constexpr int kTcMmaWarp = 4, kTcLoadWarp = 5, kTcPlaceWarp = 6;
+constexpr int kTcPlaceThreads = 64;
+// Threads of a launch: the six pipeline warps, plus the two place warps when PW (the
+// kTcPlaceWarps instantiation; a CTA that never places carries no idle warps).
+__host__ __device__ constexpr int tc_threads(bool pw) { return 32 * kTcPlaceWarp + (pw ? kTcPlaceThreads : 0); }
+
+__device__ __forceinline__ void tc_place_sync() {  // the place warps only
+  asm volatile("barrier.cta.sync 2, %0;" ::"n"(kTcPlaceThreads) : "memory");
+}
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+// Waits (bounded, like mbar_wait_bounded) until *p >= target; false when it gave up.
+__device__ __forceinline__ bool wait_flag_bounded(const uint32_t* p, uint32_t target) {
+  const uint32_t a = smem_addr(p);
+  for (int i = 0; i < kWaitPolls; ++i) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+    if (v >= target) return true;
+    __nanosleep(32);
+  }
+  return false;
+}
 
 __device__ __forceinline__ bool tc_softmax_or(bool pred) {  // OR over the 128 softmax threads
   uint32_t r;
@@ -264,8 +294,9 @@ __device__ __forceinline__ bool tc_softmax_or(bool pred) {  // OR over the 128 s
 }
 __device__ __forceinline__ void tc_softmax_sync() { asm volatile("barrier.cta.sync 1, 128;" ::: "memory"); }
 
-template <typename T, int GMAX>
-__global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __grid_constant__ TcArgs A) {
+template <typename T, int GMAX, bool PW>
+__global__ void __launch_bounds__(tc_threads(PW), 1) sink_attend_tc_kernel(const __grid_constant__ TcArgs A) {
+  constexpr int kTcThreads = tc_threads(PW);
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // swizzled tiles want 1024-byte alignment
@@ -288,6 +319,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
   int* flag = reinterpret_cast<int*>(red2 + 32);                        // CTA failure flag
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red2 + 40);
   long long* t_s = reinterpret_cast<long long*>(red2 + 42);             // place: the position t
+  // kTcPlaceWarps progress: [0] t published, [1] 1 + the last item ord whose rows are placed
+  uint32_t* pflags = reinterpret_cast<uint32_t*>(red2 + 44);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = A.group;
@@ -318,6 +351,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
     mbar_init(bar_pready + 8, kThreads);
     mbar_init(bar_mdone, 1);
     *flag = 0;
+    pflags[0] = pflags[1] = 0;
     fence_mbar_init();
   }
   __syncwarp();
@@ -343,7 +377,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
 
   grid_dependency_wait();  // the producers of q and of the cache rows are complete
 
-  if (A.place) {
+  if (A.place == kTcPlaceFirst) {  // every thread, before the pipeline starts
     if (tid == 0) *t_s = A.pa.position ? A.pa.position[0] : A.pa.t_host;
     __syncthreads();
     const long long t = *t_s;
@@ -354,16 +388,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
     }
     fence_proxy_async_global();  // the TMA loads below read the placed rows
     __syncthreads();
-    if (tid == 0 && A.pa.position) v2_position_arrive(A.pa, t);
+    if (tid == 0 && A.pa.position) v2_position_arrive(A.pa, t);  // every CTA has read t
   }
+
+  // kTcPlaceWarps: rows [a, e) of an item that the place warps write (the new token's ring
+  // slot, region rows)
+  auto slot_in = [&](long long r, const TcItem& w) { return A.pa.knew != nullptr && w.a <= r && r < w.e; };
+  auto region_in = [&](int lo, int hi) { return A.pa.R > 0 && hi > A.pa.ring && lo < A.pa.ring + A.pa.R; };
 
   bool failed = false;
   if (warp == kTcLoadWarp) {
     // ================================================================ TMA loads (one lane)
     if (lane == 0 && my_items > 0) {
+      // kTcPlaceWarps: the ring slot this step writes
+      const bool warps_place = PW && A.place == kTcPlaceWarps;
+      long long new_row = -1;
+      if (warps_place) {
+        if (!wait_flag_bounded(pflags, 1)) failed = true;
+        new_row = (*t_s - A.pa.n_sink) % A.pa.ring;
+        if (new_row < 0) new_row += A.pa.ring;
+      }
       int seq = 0;
       for (int ord = 0; ord < my_items && !failed; ++ord) {
         const TcItem w = item_of(ord);
+        bool placed = !warps_place;  // this item's placed rows are written
         const int qs = ord % kTcQSlots;
         if (A.q_async && ord >= kTcQSlots &&
             !mbar_wait_bounded(bar_qempty + 8 * qs, ((ord / kTcQSlots) - 1) & 1)) {
@@ -379,6 +427,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
         for (int c = 0; c < w.n; ++c, ++seq) {
           const int slot = seq % kTcStages, use = seq / kTcStages;
           const int row = w.a + c * kTcRows;
+          const int rend = imin(row + kTcRows, w.e);
+          if (!placed && (region_in(row, rend) || (A.pa.knew != nullptr && row <= new_row && new_row < rend))) {
+            if (!wait_flag_bounded(pflags + 1, uint32_t(ord) + 1)) {  // this chunk holds placed rows
+              failed = true;
+              break;
+            }
+            placed = true;
+          }
           if (seq >= kTcStages && !mbar_wait_bounded(bar_kempty + 8 * slot, (use - 1) & 1)) {
             failed = true;
             break;
@@ -467,6 +523,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) sink_attend_tc_kernel(const __g
       }
       tc_commit(bar_mdone);  // TMEM is freed only after every MMA has completed
       mbar_wait_bounded(bar_mdone, 0);
+    }
+  } else if (PW && warp >= kTcPlaceWarp) {
+    // ================================================================ place work (2 warps)
+    // kTcPlaceWarps: the ring-buffer step's state update for the rows of this CTA's items,
+    // item by item in the order the loads reach them (t published first).  Each item's
+    // generic stores are ordered before the loads' async-proxy reads of them by the writers'
+    // proxy fence, the place barrier and a release store the load warp acquires.
+    if (A.place == kTcPlaceWarps) {
+      const int ptid = tid - 32 * kTcPlaceWarp;
+      if (ptid == 0) {
+        *t_s = A.pa.position ? A.pa.position[0] : A.pa.t_host;
+        st_release_u32(pflags, 1);
+      }
+      tc_place_sync();
+      const long long t = *t_s;
+      const long long ws = v2_window_start(A.pa, t);
+      long long new_row = (t - A.pa.n_sink) % A.pa.ring;
+      if (new_row < 0) new_row += A.pa.ring;
+      for (int ord = 0; ord < my_items; ++ord) {
+        const TcItem w = item_of(ord);
+        if (!slot_in(new_row, w) && !region_in(w.a, w.e)) continue;
+        v2_place_pair<T, kTcD>(A.pa, w.b, w.h, t, ws, w.a, w.e, ptid, kTcPlaceThreads);
+        fence_proxy_async_global();
+        tc_place_sync();
+        if (ptid == 0) st_release_u32(pflags + 1, uint32_t(ord) + 1);
+      }
+      // every CTA has read t before it counts itself in; the last stores t + 1
+      if (ptid == 0 && A.pa.position) v2_position_arrive(A.pa, t);
     }
   } else {
     // ================================================================ softmax (4 warps)

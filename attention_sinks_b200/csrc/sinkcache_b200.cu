@@ -653,7 +653,8 @@ bool tc_cluster_merge(int dev, int ns, long items, int sms) {
 
 template <typename T, int GMAX>
 int32_t launch_tc_g(const TcArgs& A0, const Plan& pl, int pairs, cudaStream_t st, int dev, bool* merged) {
-  auto kern = sink_attend_tc_kernel<T, GMAX>;
+  const bool pw = A0.place == kTcPlaceWarps;
+  auto kern = pw ? sink_attend_tc_kernel<T, GMAX, true> : sink_attend_tc_kernel<T, GMAX, false>;
   const int32_t rc = prepare_device(dev);
   if (rc) return rc;
   const int sms = device_sms(&dev);
@@ -663,7 +664,7 @@ int32_t launch_tc_g(const TcArgs& A0, const Plan& pl, int pairs, cudaStream_t st
   TcArgs A = A0;
   *merged = tc_cluster_merge(dev, pl.ns, items, sms);
   A.cluster = *merged ? 1 : 0;
-  return launch_dependent_c(kern, dim3(grid), kTcThreads, kTcSmemBytes, *merged ? pl.ns : 1, st, A);
+  return launch_dependent_c(kern, dim3(grid), tc_threads(pw), kTcSmemBytes, *merged ? pl.ns : 1, st, A);
 }
 
 template <typename T>
@@ -680,11 +681,11 @@ int32_t launch_attention_tc(const sink_rows_t* q, const sink_kv_buffers_t* kv, i
                             float scale, const uint8_t* mask, int64_t mask_stride_b, void* out,
                             int64_t out_stride_b, int64_t out_stride_h, void* workspace,
                             const Plan& pl, int dev, cudaStream_t st,
-                            const V2PlaceArgs* place = nullptr) {
+                            const V2PlaceArgs* place = nullptr, int place_mode = kTcPlaceNone) {
   TcArgs A;
   std::memset(&A, 0, sizeof(A));
   if (place) {
-    A.place = 1;
+    A.place = place_mode;
     A.pa = *place;
   }
   int32_t rc = encode_cache_map(&A.kmap, kv->k, kv->k_dtype, kv, kv->k_stride_b, kv->k_stride_h);
@@ -738,10 +739,11 @@ int32_t launch_attention_tc(const sink_rows_t* q, const sink_kv_buffers_t* kv, i
 int32_t launch_attention(const sink_rows_t* q, const sink_kv_buffers_t* kv, int32_t rows,
                          float scale, const uint8_t* mask, int64_t mask_stride_b, void* out,
                          int64_t out_stride_b, int64_t out_stride_h, void* workspace,
-                         const Plan& pl, int dev, cudaStream_t st, const V2PlaceArgs* place = nullptr) {
+                         const Plan& pl, int dev, cudaStream_t st, const V2PlaceArgs* place = nullptr,
+                         int place_mode = kTcPlaceNone) {
   if (pl.tc)
     return launch_attention_tc(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
-                               out_stride_h, workspace, pl, dev, st, place);
+                               out_stride_h, workspace, pl, dev, st, place, place_mode);
   if (place) return SINK_EINVAL;
   int32_t rc;
   StreamArgs A;
@@ -967,10 +969,14 @@ cudaError_t allow_smem_stream() {
 template <typename T>
 cudaError_t allow_smem_tc() {
   const int b = kTcSmemBytes;
-  cudaError_t e = stream_attrs(sink_attend_tc_kernel<T, 1>, b);
-  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 2>, b);
-  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 4>, b);
-  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 8>, b);
+  cudaError_t e = stream_attrs(sink_attend_tc_kernel<T, 1, false>, b);
+  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 2, false>, b);
+  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 4, false>, b);
+  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 8, false>, b);
+  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 1, true>, b);
+  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 2, true>, b);
+  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 4, true>, b);
+  if (e == cudaSuccess) e = stream_attrs(sink_attend_tc_kernel<T, 8, true>, b);
   return e;
 }
 
@@ -983,7 +989,7 @@ void tc_cluster_capacity(int dev) {
   for (int n = 2; n <= kTcClusterMax; ++n) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(n));
-    cfg.blockDim = dim3(kTcThreads);
+    cfg.blockDim = dim3(tc_threads(false));
     cfg.dynamicSmemBytes = kTcSmemBytes;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -993,7 +999,7 @@ void tc_cluster_capacity(int dev) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, sink_attend_tc_kernel<__nv_bfloat16, 2>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&clusters, sink_attend_tc_kernel<__nv_bfloat16, 2, false>, &cfg) != cudaSuccess) {
       clusters = 0;
       (void)cudaGetLastError();
     }
@@ -1285,7 +1291,7 @@ int32_t sink_v2_place(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
   return launch_v2_place(kv, a, sms, static_cast<cudaStream_t>(stream));
 }
 
-constexpr long kFusedPlaceChunksPerCta = 32;
+constexpr long kPlaceWarpsChunksPerCta = 16;
 
 int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
                             const sink_rows_t* v_new, const sink_rows_t* region_keys,
@@ -1307,17 +1313,25 @@ int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_ne
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int sms = device_sms(&dev);
   if (sms <= 0) return SINK_EDEVICE;
-  // One launch where each tensor-core CTA places the rows of its own items first: with no
-  // more pairs than CTAs, no CTA owns more than one region item and one ring-slot item (the
-  // items of one split are consecutive).  Only for short steps: where the other CTAs keep
-  // HBM saturated for long, the owners' place loads queue behind their streams and those
-  // CTAs finish last, while the place kernel runs on an idle memory system (32,768 slots x
-  // 8 streams: 180 us fused, 176 us with the place kernel; 4,096 x 8: 37.0 against 37.9).
-  // More pairs, or more than kFusedPlaceChunksPerCta chunks per CTA, keep the place kernel.
-  const long chunks = long(a.pairs) * ((rows + kTcRows - 1) / kTcRows);
-  if (pl.tc && a.pairs <= sms && chunks <= kFusedPlaceChunksPerCta * long(sms))
-    return launch_attention(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
-                            out_stride_h, workspace, pl, dev, st, &a);
+  // One launch on the tensor-core path, each CTA placing the rows of its own items.  Long
+  // steps whose CTAs walk several items (at least kPlaceWarpsChunksPerCta chunks per CTA):
+  // two warps place item by item beside the pipeline, which waits only for the chunks
+  // holding placed rows.  Other steps with no more pairs than SMs: every thread places
+  // before the pipeline starts; split-major items put each pair's region and new-token items
+  // on different CTAs.  Short steps over more pairs keep the place kernel (one CTA per pair)
+  // before the attention: there a CTA would place several pairs' region rows on the step's
+  // critical path.
+  if (pl.tc) {
+    const long items = long(a.pairs) * pl.ns;
+    const long ctas = items < sms ? items : sms;
+    const long chunks = long(a.pairs) * ((rows + kTcRows - 1) / kTcRows);
+    int mode = kTcPlaceNone;
+    if (items > ctas && chunks >= kPlaceWarpsChunksPerCta * ctas) mode = kTcPlaceWarps;
+    else if (a.pairs <= sms) mode = kTcPlaceFirst;
+    if (mode != kTcPlaceNone)
+      return launch_attention(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
+                              out_stride_h, workspace, pl, dev, st, &a, mode);
+  }
   if ((rc = launch_v2_place(kv, a, sms, st))) return rc;
   return launch_attention(q, kv, rows, scale, mask, mask_stride_b, out, out_stride_b,
                           out_stride_h, workspace, pl, dev, st);

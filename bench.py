@@ -213,9 +213,9 @@ class OpBenchV2:
     state: a ring of window + 1 slots holding keys rotated at their absolute positions, the
     n_sink region rows (original keys at positions 0..n_sink-1), the device position far
     from the origin, plus a small pool of per-step inputs.  A step is sink_v2_decode_step:
-    the place kernel (ring write, region rotation, position advance), split-K attention over
-    the window + 1 + n_sink rows and the split combine (the place work runs inside the
-    tensor-core attention kernel when there are no more pairs than SMs)."""
+    the place work (ring write, region rotation, position advance) and split-K attention
+    over the window + 1 + n_sink rows in one tensor-core launch, then the split combine
+    unless the splits merge inside their clusters."""
 
     POOL = 4
 
@@ -904,8 +904,8 @@ def op_kinds() -> dict:
                             f"GQA decode attention over window + 1 + n_sink rows, Qwen3-0.6B layer shape "
                             f"(Hq {HQ}, Hkv {HKV}, head_dim {D})",
                    key_dtype="bf16", dtype="bf16",
-                   kernel="sink_attend_tc_kernel<bf16, 2> (tcgen05, persistent; timed with the place kernel "
-                          "and the split combine: the whole v2 step)",
+                   kernel="sink_attend_tc_kernel<bf16, 2, true> (tcgen05, persistent, place work in two of its warps; "
+                          "timed with the split combine: the whole v2 step)",
                    api="SinkLayerV2.update + decode_attention_forward (fused step)"),
     }
 

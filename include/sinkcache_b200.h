@@ -275,9 +275,10 @@ int32_t sink_v2_place(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,
  * head_dim] over the window + 1 + R rows (ring, then region) -- as sink_decode_attention,
  * with its mask convention over those rows.  Workspace: sink_workspace_bytes(SINK_OP_ATTEND,
  * ..., rows = window + 1 + R, ...).  On the tensor-core path (16-bit K and V, head_dim 128)
- * the place work runs inside the attention kernel, each CTA on the rows of its own split
- * items, so the step is one launch (plus the split combine when the splits do not fit one
- * cluster each); otherwise the place kernel runs first.  Replaces SinkLayerV2._decode_step (cache_v2.py:167-181)
+ * the place work runs inside the attention kernel, in two warps of each CTA on the rows of
+ * its own split items while the pipeline loads the other chunks, so the step is one launch
+ * (plus the split combine when the splits do not merge inside their clusters); otherwise
+ * the place kernel runs first.  Replaces SinkLayerV2._decode_step (cache_v2.py:167-181)
  * followed by decode_attention_forward over the views it returns (decode_attention.py:136-143).
  */
 int32_t sink_v2_decode_step(const sink_kv_buffers_t* kv, const sink_rows_t* k_new,

@@ -84,15 +84,20 @@ def test_place_step_matches_oracle(dtype, d, rot, t):
     (1, 16, 8, 128, 1020, 4), (4, 32, 8, 64, 300, 0), (2, 14, 2, 128, 4095, 36), (3, 8, 8, 256, 60, 1),
     (1, 16, 8, 128, 32764, 4), (32, 16, 8, 128, 4095, 4), (8, 64, 8, 128, 1020, 4),
     (8, 16, 8, 128, 32764, 4), (18, 16, 8, 128, 2047, 4), (19, 16, 8, 128, 2047, 4),
+    (64, 16, 8, 128, 252, 4), (2, 16, 8, 128, 4095, 4),
 ])
 def test_fused_decode_step_matches_place_then_attention(batch, hq, hkv, d, window, R):
     """sink_v2_decode_step leaves the cache exactly as sink_v2_place does, and its
-    attention over ring + region is within 2e-2 of fp32 attention over the same rows: with
-    the place work inside the tensor-core kernel (16-bit head_dim 128, pairs <= SMs and at
-    most 32 chunks of 128 rows per SM: 18 x 8 = 144 pairs) and on the place kernel before it
-    (19 x 8 = 152 pairs; 8 x 8 at 32,768 slots, a long step; the stream kernel at head_dim
-    64 and 256).  The launch count tells which ran: the step launches what attention over
-    the same rows launches, plus the place kernel where it is not fused."""
+    attention over ring + region is within 2e-2 of fp32 attention over the same rows, in
+    every way the step runs: on the tensor-core path (16-bit, head_dim 128) with the place
+    work in two warps beside the pipeline (CTAs walking several items, at least 16 chunks of
+    128 rows per CTA: 32 x 8 pairs at 4,096 slots, 8 x 8 at 32,768, 19 x 8 at 2,048), with
+    every thread placing first (other steps over at most one pair per SM: 18 x 8 at 2,048,
+    1 x 8 at 1,024 and 32,768, 2 x 8 at 4,096, GQA 8 and 7), and with the place kernel first
+    (64 x 8 pairs at 256 slots); on the stream kernel after the place kernel (head_dim 64
+    and 256).  The launch count tells which ran: the step
+    launches what attention over the same rows launches, plus the place kernel where it is
+    not fused."""
     g = torch.Generator().manual_seed(window + R)
     ring, dt = window + 1, torch.bfloat16
     t = 5 * window + 13
@@ -119,7 +124,10 @@ def test_fused_decode_step_matches_place_then_attention(batch, hq, hkv, d, windo
     n_attend = _lib.launch_count() - n0
     sms = _lib.sm_count(torch.device(DEV))
     pairs = batch * hkv
-    fused = d == 128 and pairs <= sms and pairs * -(-rows // 128) <= 32 * sms
+    plan = _lib.plan(_lib.OP_ATTEND, batch, hkv, hq, d, dt, dt, rows, 0, 1, 0, sms)
+    items = pairs * plan["splits"]
+    ctas = min(items, sms)
+    fused = d == 128 and ((items > ctas and pairs * -(-rows // 128) >= 16 * ctas) or pairs <= sms)
     assert n_step == n_attend + (0 if fused else 1)
     want = oracle.decode_attention(q.cpu(), ref_k[:, :, :rows].cpu(), ref_v[:, :, :rows].cpu(), d ** -0.5)
     torch.testing.assert_close(out.float().cpu(), want, rtol=0, atol=2e-2)
