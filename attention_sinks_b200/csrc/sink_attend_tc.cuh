@@ -2,7 +2,8 @@
 // with head_dim 128: the attention of the ring-buffer (v2) step and of plain decode
 // attention over model-dtype keys (src/sinkcache/decode_attention.py:29-130).
 //
-// Persistent: one CTA (192 threads) per SM (the pipeline takes 192 KB of shared memory)
+// Persistent: one CTA (192 threads; 256 with the place warps of a fused ring-buffer step)
+// per SM (the pipeline takes 192 KB of shared memory)
 // walks the work items (split, batch * kv-head) i = blockIdx.x, blockIdx.x + gridDim.x, ...
 // (tc_item) as one continuous stream of 128-row key chunks, so the copy pipeline stays full
 // across item boundaries.  Per chunk:
