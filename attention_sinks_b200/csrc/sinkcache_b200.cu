@@ -472,10 +472,12 @@ int32_t dispatch_stream(int kdt, int vdt, int D, int G, const StreamArgs& A, con
   return SINK_EDTYPE;
 }
 
-// A clustered plan whose cluster the device cannot place at all (a part or partition with
-// fewer SMs per GPC than the cluster needs) runs as the split launch of the same plan:
-// halo pre-pass, unclustered stream kernel, combine.  The workspace already holds the split
-// launch's partials and halo rows.
+// A clustered plan runs as one wave of clusters, one per pair.  Where the device holds fewer
+// of its clusters at once (cudaOccupancyMaxActiveClusters: clusters must fit a GPC, so a
+// part or partition with small GPCs holds fewer than its CTA slots suggest, or none), the
+// same plan runs as the split launch instead -- halo pre-pass, unclustered stream kernel,
+// combine -- since clusters over several waves leave CTA slots idle.  The workspace already
+// holds the split launch's partials and halo rows.
 template <bool ATTEND>
 int32_t settle_cluster(const sink_kv_buffers_t* kv, int G, StreamArgs& A, Plan& pl, int pairs,
                        cudaStream_t st, int dev) {
@@ -484,7 +486,7 @@ int32_t settle_cluster(const sink_kv_buffers_t* kv, int G, StreamArgs& A, Plan& 
   const int32_t rc = dispatch_stream<ATTEND>(kv->k_dtype, kv->v_dtype, kv->head_dim, G, A, pl, pairs, st, dev,
                                              &capacity);
   if (rc) return rc;
-  if (capacity < 1) {
+  if (capacity < pairs) {
     pl.cluster = false;
     A.cluster = 0;
   }

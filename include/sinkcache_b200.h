@@ -307,11 +307,11 @@ int32_t sink_debug_fail_next_wait(int32_t chunk, int32_t polls);
 
 /*
  * Test hook for the cluster fallback: clusters >= 0 is taken as the number of clusters the
- * device can hold at once for every clustered stream launch of the process (0: none can be
- * placed, so clustered plans run as split launches -- halo pre-pass, stream kernel, combine
- * -- with the same splits); -1 (the default) asks the device (cudaOccupancyMaxActiveClusters,
- * once per kernel and cluster size, outside stream capture).  Launches nothing.  Returns 0,
- * or SINK_EINVAL for clusters < -1.
+ * device can hold at once for every clustered stream launch of the process (a clustered plan
+ * needs one per (batch, head) pair in one wave; with fewer -- 0: none can be placed -- it runs
+ * as the split launch: halo pre-pass, stream kernel, combine, with the same splits); -1 (the
+ * default) asks the device (cudaOccupancyMaxActiveClusters, once per kernel and cluster size,
+ * outside stream capture).  Launches nothing.  Returns 0, or SINK_EINVAL for clusters < -1.
  */
 int32_t sink_debug_cluster_capacity(int32_t clusters);
 

@@ -289,6 +289,33 @@ def test_cluster_fallback_runs_the_plan_split(op, drop, launches, built_lib):
     torch.testing.assert_close(oa.float(), ob.float(), rtol=0, atol=1e-2)
 
 
+@pytest.mark.parametrize("batch,slots,launches", [(1, 256, 1), (8, 256, 1), (1, 1024, 1), (8, 1024, 1),
+                                                 (7, 4096, 1), (2, 2047, 3)])
+def test_planned_clusters_launch_as_one_wave(batch, slots, launches, built_lib):
+    """The small fused steps the planner clusters (clusters of 3 to 16 CTAs, one per (batch,
+    head) pair) stay a single launch where the B200 holds all their clusters at once by its
+    own count; 16 clusters of 16 CTAs (2,048 slots x 2 streams) do not fit one wave there
+    (a cluster must fit one GPC), so that step runs split: halo pre-pass, stream kernel,
+    combine."""
+    f32, bf = torch.float32, torch.bfloat16
+    hkv, hq, d, n_sink, window = 8, 16, 128, 4, slots - 4
+    p = _lib.plan(_lib.OP_FUSED_STEP, batch, hkv, hq, d, f32, bf, slots + 1, n_sink, window, 1,
+                  _lib.sm_count(torch.device(DEV)))
+    assert p["cluster_ctas"] > 1
+    g = torch.Generator().manual_seed(slots + batch)
+    k = torch.randn(batch, hkv, slots + 1, d, generator=g).to(DEV)
+    v = torch.randn(batch, hkv, slots + 1, d, generator=g).bfloat16().to(DEV)
+    k1, v1 = [torch.randn(batch, hkv, 1, d, generator=g).bfloat16().to(DEV) for _ in range(2)]
+    q = torch.randn(batch, hq, 1, d, generator=g).bfloat16().to(DEV)
+    cos, sin = [t.to(DEV) for t in oracle.rope_cos_sin(torch.tensor(-1), cases.inv_freq(d, 1e6))]
+    out = torch.empty(batch, 1, hq, d, dtype=bf, device=DEV)
+    ws = _lib.Workspace()
+    n0 = _lib.launch_count()
+    _lib.fused_decode_step(k, v, k1, v1, q, n_sink, window, 1, slots, cos, sin, d ** -0.5, out, ws)
+    assert _lib.launch_count() - n0 == launches
+    _status_clean(ws)
+
+
 def _masked_oracle(q, k, v, mask, scale):
     """Attention per stream over the rows its boolean mask keeps."""
     outs = []
