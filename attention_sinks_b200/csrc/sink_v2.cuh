@@ -35,25 +35,21 @@ __device__ __forceinline__ long long v2_window_start(const V2PlaceArgs& a, long 
   return ws;
 }
 
-// Parts of the place work (v2_place_pair's `parts`).
-constexpr int kPlaceSlot = 1, kPlaceRegion = 2;
-
 // The place work of one (batch, kv-head) pair, limited to its rows [row_lo, row_hi) of the
 // kv buffers (ring slots, then the region rows from `ring`): the new token into ring slot
-// (t - n_sink) mod ring when that slot is in range (kPlaceSlot), and the region rows j (kv
-// row ring + j, or region_out row j) in range rotated from their originals (kPlaceRegion).  Region row j is rotated by
+// (t - n_sink) mod ring when that slot is in range, and the region rows j (kv row ring + j,
+// or region_out row j) in range rotated from their originals.  Region row j is rotated by
 // (ws - R + j) - reg_pos[j]; the angle is formed in fp64 (positions grow without bound),
 // cos/sin rounded once to fp32, and each output element is fp32(fp32(x * cos) +
 // fp32(rotate_half(x) * sin)) rounded once to the storage type: the reference's three
 // separately rounded tensor ops.  Threads `tid` of `nthreads` share the work.
 template <typename T, int D>
 __device__ __forceinline__ void v2_place_pair(const V2PlaceArgs& a, int b, int h, long long t, long long ws,
-                                              int row_lo, int row_hi, int tid, int nthreads,
-                                              int parts = kPlaceSlot | kPlaceRegion) {
+                                              int row_lo, int row_hi, int tid, int nthreads) {
   using E = Elem<T>;
   constexpr int kVec = 16 / sizeof(T);   // elements per 16-byte vector
   constexpr int kRowVecs = D / kVec;
-  if (a.knew && (parts & kPlaceSlot)) {
+  if (a.knew) {
     long long slot = (t - a.n_sink) % a.ring;
     if (slot < 0) slot += a.ring;
     if (slot >= row_lo && slot < row_hi) {
@@ -70,7 +66,7 @@ __device__ __forceinline__ void v2_place_pair(const V2PlaceArgs& a, int b, int h
   }
   const int j0 = row_lo - a.ring > 0 ? row_lo - a.ring : 0;
   const int j1 = row_hi - a.ring < a.R ? row_hi - a.ring : a.R;
-  if (!(parts & kPlaceRegion) || j0 >= j1) return;
+  if (j0 >= j1) return;
   const T* rk = reinterpret_cast<const T*>(a.reg_k) + b * a.rk_sb + h * a.rk_sh;
   T* ro = reinterpret_cast<T*>(a.rout) + b * a.ro_sb + h * a.ro_sh;
   const int rh = a.rot_half, pass = D - 2 * rh;
