@@ -78,8 +78,10 @@ __device__ __forceinline__ void v2_place_pair(const V2PlaceArgs& a, int b, int h
     if (c < rh) {
       const long long delta = ws - a.R + j - a.reg_pos[j];
       const double ang = __dmul_rn(static_cast<double>(delta), a.inv_freq[c]);
-      const float cs = __double2float_rn(cos(ang));
-      const float sn = __double2float_rn(sin(ang));
+      double sd, cd;
+      sincos(ang, &sd, &cd);  // one argument reduction for both
+      const float cs = __double2float_rn(cd);
+      const float sn = __double2float_rn(sd);
       const float x1 = E::to_f(x[c]), x2 = E::to_f(x[c + rh]);
       y[c] = E::from_f(__fadd_rn(__fmul_rn(x1, cs), __fmul_rn(-x2, sn)));
       y[c + rh] = E::from_f(__fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn)));
